@@ -1,0 +1,377 @@
+"""Benchmark: Q4_K / Q6_K integer matvec HBM GB/s on B200, bit-exact.
+
+python bench.py [--gpus N] [--steps K] [--warmup W] [--impl vtq|reference] [--config NAME]
+
+A step is one pass of the hot path over one batch: every matvec of the
+configuration (default c2: Llama-7B FFN Q4_K, 4096->11008 and 11008->4096,
+batch 1). `value` is algorithmic bytes (packed weights + 4*in + 4*out per
+matvec) / device time, with the weights resident in HBM. Between steps the
+weights rotate over enough distinct copies that the set read per rotation
+exceeds the 126 MB L2, so no step is served from L2.
+
+`e2e` is the same metric through the public C ABI (vtq_linear with VTQ_PTR_HOST):
+every step copies x from pinned host memory, runs the kernel and reads y back.
+
+N > 1 (torchrun, one rank per GPU): weak scaling -- every rank streams its own
+weights for the same per-rank workload; no data-path collective (rows are
+independent). Timing is bracketed by barrier + synchronize and the max over
+ranks is taken.
+
+--impl reference times the reference's CPU path (the oracle port of
+linear_q4_k_integer_parallel / linear_q6_k_integer_parallel: the reference is
+Rust and no Rust toolchain exists on this image) on the host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+import numpy as np
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(REPO, "vitni-tensor_b200"))
+sys.path.insert(0, REPO)
+
+METRIC = "Q4_K/Q6_K matvec HBM GB/s (% of peak), bit-exact; decode tok/s at 1-8 B200"
+L2_BYTES = 126 * 1024 * 1024
+ROTATE_MIN_BYTES = 2 * L2_BYTES
+
+
+def algo_bytes(dtype, n, r, batch=1):
+    import vtq
+    return r * vtq.row_bytes(dtype, n) + 4 * n * batch + 4 * r * batch
+
+
+def peaks():
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def profile_traffic(cfg):
+    """dram bytes per launch of the dominant kernel from the committed ncu summary."""
+    path = os.path.join(REPO, "profiles", f"kq_matvec_{cfg}.md")
+    try:
+        for line in open(path):
+            if line.startswith("dram_bytes_per_launch:"):
+                return float(line.split(":")[1])
+    except OSError:
+        pass
+    return None
+
+
+class ClockSampler:
+    """NVML clocks / throttle reasons sampled in a thread during the timed region."""
+
+    REASONS = {0x8: "hw_slowdown", 0x40: "hw_thermal_slowdown", 0x20: "sw_thermal_slowdown",
+               0x4: "sw_power_cap", 0x80: "hw_power_brake_slowdown", 0x1: "gpu_idle",
+               0x2: "applications_clocks_setting", 0x10: "sync_boost",
+               0x100: "display_clock_setting"}
+
+    def __init__(self, device_index):
+        self.samples, self.reasons = [], 0
+        self.ok = False
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception:
+            self.max_mhz = None
+        self._stop = threading.Event()
+
+    def _sample(self):
+        self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+        self.reasons |= self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self._sample()
+            except Exception:
+                return
+            time.sleep(0.002)
+
+    def start(self):
+        if self.ok:
+            self.t = threading.Thread(target=self._run, daemon=True)
+            self.t.start()
+
+    def stop(self):
+        if not self.ok:
+            return None
+        self._stop.set()
+        self.t.join()
+        try:
+            self._sample()
+        except Exception:
+            pass
+        names = sorted(v for k, v in self.REASONS.items() if self.reasons & k and v != "gpu_idle")
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
+                "sm_max_mhz": self.max_mhz, "reasons": names, "samples": len(self.samples)}
+
+
+def setup_dist():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def run_reference(args, world, rank):
+    """CPU reference arm (oracle port of the reference's parallel bench path)."""
+    if rank != 0:
+        return
+    from vtq import synth
+    from oracle import oracle as O
+    cfg = synth.CONFIGS[args.config]
+    mats = [(dt, n, r, synth.weight(dt, f"{args.config}.w.{n}x{r}", r, n),
+             synth.activation(f"{args.config}.x.{n}", 1, n)) for dt, n, r in cfg]
+    threads = os.cpu_count() or 1
+    name = {12: "q4_k_integer", 14: "q6_k_integer", 8: None}
+    step_bytes = sum(algo_bytes(dt, n, r) for dt, n, r in cfg)
+
+    def step():
+        for dt, n, r, w, x in mats:
+            if name.get(dt):
+                O.linear(name[dt], x, w, 1, n, r, threads)
+            else:
+                O.linear_dispatch(dt, x, w, n, r, threads=threads)
+
+    for _ in range(max(1, args.warmup)):
+        step()
+    times = []
+    for _ in range(max(1, args.steps)):
+        t0 = time.perf_counter()
+        step()
+        times.append(time.perf_counter() - t0)
+    total = sum(times)
+    value = step_bytes * len(times) / total / 1e9
+    line = {
+        "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "impl": "reference",
+        "n_gpus": world, "steps": len(times), "warmup": args.warmup,
+        "ms_per_step": round(1e3 * total / len(times), 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+        "config": {"workload": args.config, "batch": 1, "l2": "host run"},
+        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads,
+                         "kind": "port",
+                         "sample": f"{len(times)} full steps of {args.config} on {threads} "
+                                   "threads (oracle restatement of linear_*_integer_parallel)"},
+        "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def cpu_baseline(cfg_name, budget_s=12.0):
+    """Oracle timed on the host cores on a bounded sample of the workload."""
+    from vtq import synth
+    from oracle import oracle as O
+    cfg = synth.CONFIGS[cfg_name]
+    threads = os.cpu_count() or 1
+    mats = [(dt, n, r, synth.weight(dt, f"{cfg_name}.w.{n}x{r}", r, n),
+             synth.activation(f"{cfg_name}.x.{n}", 1, n)) for dt, n, r in cfg]
+    name = {12: "q4_k_integer", 14: "q6_k_integer"}
+    nbytes = 0
+    t0 = time.perf_counter()
+    t_end = t0 + budget_s
+    steps = 0
+    while time.perf_counter() < t_end or steps == 0:
+        for dt, n, r, w, x in mats:
+            if dt in name:
+                O.linear(name[dt], x, w, 1, n, r, threads)
+            else:
+                O.linear_dispatch(dt, x, w, n, r, threads=threads)
+            nbytes += algo_bytes(dt, n, r)
+        steps += 1
+    el = time.perf_counter() - t0
+    return {"value": round(nbytes / el / 1e9, 3), "unit": "GB/s", "cores": threads,
+            "kind": "port",
+            "sample": f"{steps} full steps of {cfg_name} in {el:.1f} s, {threads} threads "
+                      "(oracle restatement of the reference's row-parallel integer linears)"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=3000)
+    ap.add_argument("--warmup", type=int, default=50)
+    ap.add_argument("--impl", default="vtq", choices=["vtq", "reference"])
+    ap.add_argument("--config", default="c2_q4_k_llama7b_ffn")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--check", action="store_true", help="bit-compare outputs with the oracle")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+    world, rank, local = setup_dist()
+
+    if args.impl == "reference":
+        run_reference(args, world, rank)
+        return
+
+    import torch
+    import torch.distributed as dist
+    import vtq
+    from vtq import synth
+
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    ctx = vtq.Context(local)
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    ctx.set_stream(stream.cuda_stream)
+
+    cfg = synth.CONFIGS[args.config]
+    step_bytes = sum(algo_bytes(dt, n, r) for dt, n, r in cfg)
+    wbytes = sum(r * vtq.row_bytes(dt, n) for dt, n, r in cfg)
+    copies = max(1, -(-ROTATE_MIN_BYTES // wbytes))
+    host_w = [synth.weight(dt, f"{args.config}.w.{n}x{r}", r, n) for dt, n, r in cfg]
+    host_x = [synth.activation(f"{args.config}.x.{n}", 1, n) for dt, n, r in cfg]
+    weights = [[ctx.upload(dt, host_w[i], n, r) for i, (dt, n, r) in enumerate(cfg)]
+               for _ in range(copies)]
+    xs = [torch.from_numpy(x).cuda() for x in host_x]
+    ys = [torch.empty(r, device="cuda") for dt, n, r in cfg]
+
+    # Capture one rotation (copies x matvecs) as a CUDA graph; launches per
+    # graph replay = copies * len(cfg) kernels of ours.
+    def rotation(events=None):
+        for c in range(copies):
+            for i in range(len(cfg)):
+                if events is not None:
+                    events[c * len(cfg) + i][0].record(stream)
+                ctx.linear_ptr(weights[c][i], xs[i].data_ptr(), ys[i].data_ptr(), 1)
+                if events is not None:
+                    events[c * len(cfg) + i][1].record(stream)
+
+    rotation()
+    torch.cuda.synchronize()
+    if args.check:
+        from oracle import oracle as O
+        for i, (dt, n, r) in enumerate(cfg):
+            ref = O.linear({12: "q4_k_integer", 14: "q6_k_integer"}[dt], host_x[i], host_w[i],
+                           1, n, r, os.cpu_count()) if dt in (12, 14) else \
+                O.linear_dispatch(dt, host_x[i], host_w[i], n, r, threads=os.cpu_count())
+            got = ys[i].cpu().numpy()
+            assert np.array_equal(got.view(np.uint32), ref.view(np.uint32)), "parity failure"
+
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream, capture_error_mode="thread_local"):
+        rotation()
+    launches_per_replay = copies * len(cfg)
+    replays = max(1, -(-args.steps // (copies)))  # each replay = `copies` steps
+    steps = replays * copies
+    warm_replays = max(1, -(-args.warmup // copies))
+    for _ in range(warm_replays):
+        g.replay()
+    torch.cuda.synchronize()
+
+    # ---- timed region (device time, events on the launching stream) ----
+    clocks = ClockSampler(local)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(replays):
+        g.replay()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    if world > 1:
+        dist.barrier()
+    ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    value = step_bytes * steps * world / (ms / 1e3) / 1e9
+
+    # ---- per-launch durations of the dominant kernel (same stream, graph-free) ----
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(launches_per_replay)]
+    durs = []
+    for _ in range(max(3, 300 // launches_per_replay)):
+        rotation(evs)
+        torch.cuda.synchronize()
+        durs += [a.elapsed_time(b) for a, b in evs]
+    per_launch_bytes = statistics.mean(
+        [algo_bytes(dt, n, r) for dt, n, r in cfg])
+    avg_ms = statistics.mean(durs)
+    peak, peak_kind = peaks()
+    achieved = per_launch_bytes / (avg_ms / 1e3) / 1e9
+    traffic = profile_traffic(args.config)
+
+    # ---- e2e through the public C ABI with host buffers ----
+    px = [torch.from_numpy(x).pin_memory() for x in host_x]
+    py = [torch.empty(r, dtype=torch.float32).pin_memory() for dt, n, r in cfg]
+    e2e_steps = max(20, min(2000, steps // 4))
+    for _ in range(5):
+        for i in range(len(cfg)):
+            ctx.linear_ptr(weights[0][i], px[i].data_ptr(), py[i].data_ptr(), 1, host=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(stream)
+    for s in range(e2e_steps):
+        c = s % copies
+        for i in range(len(cfg)):
+            ctx.linear_ptr(weights[c][i], px[i].data_ptr(), py[i].data_ptr(), 1, host=True)
+    f1.record(stream)
+    torch.cuda.synchronize()
+    ems = f0.elapsed_time(f1)
+    if world > 1:
+        t = torch.tensor([ems], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ems = float(t.item())
+    e2e_value = step_bytes * e2e_steps * world / (ems / 1e3) / 1e9
+    h2d = sum(4 * n for dt, n, r in cfg)
+    d2h = sum(4 * r + 256 for dt, n, r in cfg)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(args.config)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+            "steps": steps, "warmup": warm_replays * copies,
+            "ms_per_step": round(ms / steps, 5), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "config": {"workload": args.config,
+                       "matvecs": [f"{vtq.formats.NAMES[dt]} {n}->{r}" for dt, n, r in cfg],
+                       "batch": 1, "parallelism": f"replicas x{world}" if world > 1 else "1 GPU",
+                       "l2": f"inputs larger than L2: {copies} rotating weight copies "
+                             f"({copies * wbytes / 1e6:.0f} MB)",
+                       "timing": "CUDA graph of one rotation, replayed; CUDA events"},
+            "pct_of_peak": round(100 * value / world / peak, 1),
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                         "unit": "GB/s", "frac": round(achieved / peak, 4),
+                         "traffic": traffic, "peak_source": peak_kind,
+                         "kernel": "kq_matvec_kernel",
+                         "bytes_per_launch": per_launch_bytes,
+                         "avg_launch_us": round(avg_ms * 1e3, 3)},
+            "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "steps": e2e_steps},
+            "gpu_launches": steps * len(cfg),
+            "clocks": clk,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

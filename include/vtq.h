@@ -1,0 +1,134 @@
+/*
+ * vtq.h -- C ABI of the B200 (sm_100a) k-quant linear backend for vitni-tensor.
+ *
+ * Drop-in for the reference's quantized linear seam: every output is
+ * bit-identical to the reference CPU path on the same inputs. Plain C types
+ * only; every call returns a vtq_status. Citations are file:line in the
+ * vitni-tensor project (Rust).
+ *
+ * Threading: one vtq_ctx per host thread. Calls on one context are
+ * serialised on that context's CUDA stream.
+ */
+#ifndef VTQ_H
+#define VTQ_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. They map 1:1 onto the reference's error enum
+ * (src/error.rs:7-63) where one exists. */
+typedef int32_t vtq_status;
+#define VTQ_OK 0
+#define VTQ_ERR_INTERNAL 1        /* Error::Internal(&str): shape / length checks (quant.rs:944-949) */
+#define VTQ_ERR_NOT_IMPLEMENTED 2 /* Error::NotImplemented{op,why} (forward_quantized.rs:777-782) */
+#define VTQ_ERR_GPU 3             /* Error::GpuError(&str): a CUDA call failed */
+#define VTQ_ERR_OOM 4             /* Error::OutOfMemory: device allocation failed */
+#define VTQ_ERR_TIMEOUT 5         /* a bounded device-side wait ran out (no reference counterpart) */
+#define VTQ_ERR_INVALID_ARG 6     /* null pointer / bad handle (no reference counterpart: Rust slices) */
+#define VTQ_ERR_MALFORMED 7       /* Error::Malformed(&str): GGUF parse */
+#define VTQ_ERR_TRUNCATED 8       /* Error::Truncated(&str): GGUF parse */
+
+/* GGML tensor type tags (src/model/gguf.rs:127-139). */
+#define VTQ_F32 0
+#define VTQ_Q4_0 2
+#define VTQ_Q5_0 6
+#define VTQ_Q8_0 8
+#define VTQ_Q4_K 12
+#define VTQ_Q6_K 14
+
+/* vtq_linear flags. */
+#define VTQ_PTR_HOST 1u  /* x and y are host pointers; the call copies x in and y out and returns
+                            when y is written. Otherwise x/y are device pointers and the call is
+                            asynchronous on the context stream. */
+#define VTQ_Q4K_FLOAT 2u /* Q4_K in the reference's default-feature regime (float-fused canonical,
+                            quant.rs:616-702) instead of the `std-parallel` integer regime. */
+
+typedef struct vtq_ctx vtq_ctx;
+typedef struct vtq_weight vtq_weight;
+
+/* Context: one CUDA device, one stream, a device status word.
+ * No reference counterpart (the reference's CPU path has no device state). */
+vtq_status vtq_init(int device, vtq_ctx** out);
+vtq_status vtq_destroy(vtq_ctx* ctx);
+/* Message of the last failed call on this context ("" if none). */
+const char* vtq_last_error(const vtq_ctx* ctx);
+/* Use the caller's cudaStream_t (NULL = the context's own stream). */
+vtq_status vtq_set_stream(vtq_ctx* ctx, void* cuda_stream);
+vtq_status vtq_synchronize(vtq_ctx* ctx);
+
+/* Upload rows [row_begin, row_end) of a row-major GGUF weight matrix
+ * (QuantTensor bytes, src/model/quant_weights.rs:47-52; shape [out][in] in
+ * row-major terms) to device memory in the kernels' layout. `bytes` holds the
+ * whole matrix (out_feat rows). row_end = -1 means out_feat.
+ * Replaces the reference's zero-copy borrow of the GGUF blob
+ * (quant_weights.rs:121-181): the weight is resident for the handle's life. */
+vtq_status vtq_weight_upload(vtq_ctx* ctx, int32_t dtype, const uint8_t* bytes, size_t nbytes,
+                             int64_t in_feat, int64_t out_feat, int64_t row_begin,
+                             int64_t row_end, vtq_weight** out);
+vtq_status vtq_weight_free(vtq_weight* w);
+vtq_status vtq_weight_info(const vtq_weight* w, int32_t* dtype, int64_t* in_feat,
+                           int64_t* rows, size_t* device_bytes);
+
+/* y[b][r] = row r of the uploaded weight against x[b] for b < batch;
+ * x is [batch][in_feat], y is [batch][rows]. Arithmetic by dtype exactly as
+ * linear_dispatch (src/model/forward_quantized.rs:663-785):
+ *   Q4_K  integer (linear_q4_k_integer(_parallel), quant.rs:936/:1149), or
+ *         float-fused with VTQ_Q4K_FLOAT (linear_q4_k_fused, quant.rs:1433)
+ *   Q6_K  integer (linear_q6_k_integer(_parallel), quant.rs:1060/:1099)
+ *   Q8_0, Q5_0  dequantize row + canonical_dot (forward_quantized.rs:751-776)
+ *   Q4_0  linear_q4_0_cpu (quant.rs:1529)
+ *   F32   canonical_dot per row (forward_quantized.rs:674-697)
+ * The reference's row-parallel variants are bit-identical to the serial ones,
+ * so there is no thread-count argument. */
+vtq_status vtq_linear(vtq_ctx* ctx, const vtq_weight* w, const float* x, float* y, int64_t batch,
+                      uint32_t flags);
+
+/* linear_dispatch with host slices (src/model/forward_quantized.rs:663-668,
+ * batch 1): uploads `w` on every call. For parity tests and one-off calls;
+ * resident weights go through vtq_weight_upload + vtq_linear. */
+vtq_status vtq_linear_dispatch(vtq_ctx* ctx, int32_t dtype, const float* x, const uint8_t* w,
+                               size_t wlen, size_t in_feat, size_t out_feat, float* y,
+                               uint32_t flags);
+
+/* The op-level signature the reference's linears share,
+ * fn(x, w, y_out, batch, in_feat, out_feat) -> Result<()>, host slices:
+ *   vtq_linear_q4_k_integer   replaces linear_q4_k_integer(_parallel) quant.rs:936 / :1149
+ *   vtq_linear_q6_k_integer   replaces linear_q6_k_integer(_parallel) quant.rs:1060 / :1099
+ *   vtq_linear_q4_k_fused     replaces linear_q4_k_fused(_parallel)   quant.rs:1433 / :1385
+ *   vtq_linear_q4_0           replaces linear_q4_0_cpu                quant.rs:1529 */
+vtq_status vtq_linear_q4_k_integer(vtq_ctx* ctx, const float* x, const uint8_t* w, size_t wlen,
+                                   float* y, size_t batch, size_t in_feat, size_t out_feat);
+vtq_status vtq_linear_q6_k_integer(vtq_ctx* ctx, const float* x, const uint8_t* w, size_t wlen,
+                                   float* y, size_t batch, size_t in_feat, size_t out_feat);
+vtq_status vtq_linear_q4_k_fused(vtq_ctx* ctx, const float* x, const uint8_t* w, size_t wlen,
+                                 float* y, size_t batch, size_t in_feat, size_t out_feat);
+vtq_status vtq_linear_q4_0(vtq_ctx* ctx, const float* x, const uint8_t* w, size_t wlen, float* y,
+                           size_t batch, size_t in_feat, size_t out_feat);
+
+/* ---- Context-free device API (for embedding in a host that owns memory and
+ * streams). No allocation inside. ---- */
+
+/* Bytes of the device layout for `rows` rows (rows re-pitched to 16 B, plus
+ * a 16-byte tail pad). -1 if in_feat is invalid for dtype. No reference
+ * counterpart: the reference borrows GGUF bytes in place. */
+int64_t vtq_device_layout_bytes(int32_t dtype, int64_t in_feat, int64_t rows);
+/* Convert `rows` packed GGUF rows already in device memory (src_dev) into the
+ * device layout at dst_dev (vtq_device_layout_bytes bytes). Async on stream. */
+vtq_status vtq_device_repack(int32_t dtype, int64_t in_feat, int64_t rows, const uint8_t* src_dev,
+                             uint8_t* dst_dev, void* cuda_stream);
+/* Same arithmetic as vtq_linear on device pointers, async on `cuda_stream`.
+ * w_dev: device layout from vtq_device_repack. status_dev: optional device
+ * word; kernels OR in 1 if a bounded wait timed out. */
+vtq_status vtq_linear_device(int32_t dtype, const uint8_t* w_dev, int64_t in_feat, int64_t rows,
+                             const float* x_dev, int64_t ldx, float* y_dev, int64_t ldy,
+                             int64_t batch, uint32_t flags, uint32_t* status_dev,
+                             void* cuda_stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* VTQ_H */

@@ -1,0 +1,398 @@
+// vtq_api.cu -- the C ABI (include/vtq.h): contexts, resident weights,
+// linear_dispatch-shaped entry points, and the context-free device API.
+//
+// Validation and error messages follow the reference functions each entry
+// point replaces (vitni-tensor src/ops/quant.rs, src/model/forward_quantized.rs)
+// so a caller sees the same failure for the same bad input. There is no CPU
+// fallback: every arithmetic result comes from the sm_100a kernels.
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+#include "../../include/vtq.h"
+#include "vtq_internal.h"
+
+using namespace vtq;
+
+struct vtq_ctx {
+  int device = 0;
+  cudaStream_t own = nullptr;
+  cudaStream_t stream = nullptr;
+  // io buffer: [status word | 252 B pad][y capacity][x capacity]
+  uint8_t* io = nullptr;
+  size_t io_cap = 0;
+  std::string err;
+};
+
+struct vtq_weight {
+  vtq_ctx* ctx = nullptr;
+  DevMatrix m{};
+  uint8_t* buf = nullptr;
+  size_t bytes = 0;
+};
+
+namespace {
+
+constexpr size_t kStatusBytes = 256;
+
+vtq_status fail(vtq_ctx* c, vtq_status s, const std::string& msg) {
+  if (c) c->err = msg;
+  return s;
+}
+
+vtq_status gpu_fail(vtq_ctx* c, cudaError_t e, const char* where) {
+  const vtq_status s = (e == cudaErrorMemoryAllocation) ? VTQ_ERR_OOM : VTQ_ERR_GPU;
+  char b[256];
+  snprintf(b, sizeof b, "gpu error: %s: %s", where, cudaGetErrorString(e));
+  return fail(c, s, b);
+}
+
+#define VTQ_CUDA(c, call)                                    \
+  do {                                                       \
+    cudaError_t e_ = (call);                                 \
+    if (e_ != cudaSuccess) return gpu_fail((c), e_, #call);  \
+  } while (0)
+
+vtq_status ensure_io(vtq_ctx* c, size_t need) {
+  if (need <= c->io_cap) return VTQ_OK;
+  size_t cap = std::max(need, c->io_cap * 2);
+  cap = (cap + 4095) / 4096 * 4096;
+  if (c->io) {
+    VTQ_CUDA(c, cudaStreamSynchronize(c->stream));
+    cudaFree(c->io);
+    c->io = nullptr;
+    c->io_cap = 0;
+  }
+  VTQ_CUDA(c, cudaMalloc(&c->io, cap));
+  VTQ_CUDA(c, cudaMemsetAsync(c->io, 0, kStatusBytes, c->stream));
+  c->io_cap = cap;
+  return VTQ_OK;
+}
+
+bool dtype_supported(int dtype) {
+  return dtype == T_F32 || dtype == T_Q4_0 || dtype == T_Q5_0 || dtype == T_Q8_0 ||
+         dtype == T_Q4_K || dtype == T_Q6_K;
+}
+
+// Launch the kernel that implements dtype's linear_dispatch arm.
+cudaError_t run_linear(const DevMatrix& m, const float* x, int64_t ldx, float* y, int64_t ldy,
+                       int64_t batch, uint32_t flags, unsigned* status, cudaStream_t st) {
+  if (m.dtype == T_Q6_K || (m.dtype == T_Q4_K && !(flags & VTQ_Q4K_FLOAT)))
+    return launch_kq_matvec(m, x, ldx, batch, y, ldy, status, st);
+  return launch_canon_matvec(m, x, ldx, batch, y, ldy, status, st);
+}
+
+// Kernel-side limits (shared-memory residency of one activation row set).
+vtq_status check_kernel_limits(vtq_ctx* c, const DevMatrix& m, uint32_t flags) {
+  const bool integer = m.dtype == T_Q6_K || (m.dtype == T_Q4_K && !(flags & VTQ_Q4K_FLOAT));
+  if (m.in_feat > 32768)
+    return fail(c, VTQ_ERR_NOT_IMPLEMENTED,
+                std::string("vtq_linear: not implemented (in_feat > 32768 on the ") +
+                    (integer ? "integer" : "canonical") + " kernel)");
+  if (m.out_feat > INT32_MAX) return fail(c, VTQ_ERR_NOT_IMPLEMENTED, "vtq_linear: out_feat too large");
+  return VTQ_OK;
+}
+
+// Host-pointer linear on a device-resident matrix: x in, kernel, y+status out.
+vtq_status linear_host(vtq_ctx* c, const DevMatrix& m, const float* x, float* y, int64_t batch,
+                       uint32_t flags) {
+  if (vtq_status s = check_kernel_limits(c, m, flags)) return s;
+  const size_t ybytes = (size_t)batch * m.out_feat * 4, xbytes = (size_t)batch * m.in_feat * 4;
+  const size_t yoff = kStatusBytes, xoff = (yoff + ybytes + 255) / 256 * 256;
+  if (vtq_status s = ensure_io(c, xoff + xbytes)) return s;
+  float* dx = reinterpret_cast<float*>(c->io + xoff);
+  float* dy = reinterpret_cast<float*>(c->io + yoff);
+  unsigned* dstat = reinterpret_cast<unsigned*>(c->io);
+  VTQ_CUDA(c, cudaMemcpyAsync(dx, x, xbytes, cudaMemcpyHostToDevice, c->stream));
+  VTQ_CUDA(c, run_linear(m, dx, m.in_feat, dy, m.out_feat, batch, flags, dstat, c->stream));
+  // One D2H copy brings back the status word and y together.
+  std::string tmp;
+  const size_t back = yoff + ybytes;
+  uint32_t statbuf[kStatusBytes / 4];
+  if (back <= 64 * 1024) {
+    uint8_t host[64 * 1024];
+    VTQ_CUDA(c, cudaMemcpyAsync(host, c->io, back, cudaMemcpyDeviceToHost, c->stream));
+    VTQ_CUDA(c, cudaStreamSynchronize(c->stream));
+    memcpy(statbuf, host, kStatusBytes);
+    memcpy(y, host + yoff, ybytes);
+  } else {
+    VTQ_CUDA(c, cudaMemcpyAsync(statbuf, c->io, kStatusBytes, cudaMemcpyDeviceToHost, c->stream));
+    VTQ_CUDA(c, cudaMemcpyAsync(y, dy, ybytes, cudaMemcpyDeviceToHost, c->stream));
+    VTQ_CUDA(c, cudaStreamSynchronize(c->stream));
+  }
+  if (statbuf[0] != 0) {
+    VTQ_CUDA(c, cudaMemsetAsync(c->io, 0, 4, c->stream));
+    return fail(c, VTQ_ERR_TIMEOUT, "vtq_linear: a device-side wait timed out");
+  }
+  return VTQ_OK;
+}
+
+// Upload `rows` packed rows from host bytes into a fresh device matrix.
+vtq_status upload(vtq_ctx* c, int dtype, const uint8_t* bytes, int64_t in_feat, int64_t row0,
+                  int64_t rows, vtq_weight** out) {
+  auto* w = new vtq_weight();
+  w->ctx = c;
+  w->m.dtype = dtype;
+  w->m.in_feat = in_feat;
+  w->m.out_feat = rows;
+  w->m.row_bytes = packed_row_bytes(dtype, in_feat);
+  w->m.pitch = device_pitch(dtype, in_feat);
+  w->bytes = (size_t)vtq_device_layout_bytes(dtype, in_feat, rows);
+  cudaError_t e = cudaMalloc(&w->buf, std::max<size_t>(w->bytes, 256));
+  if (e != cudaSuccess) {
+    delete w;
+    return gpu_fail(c, e, "cudaMalloc(weight)");
+  }
+  w->m.data = w->buf;
+  const size_t raw = (size_t)rows * w->m.row_bytes;
+  uint8_t* staging = nullptr;
+  if (raw) {
+    e = cudaMallocAsync(&staging, raw, c->stream);
+    if (e == cudaSuccess)
+      e = cudaMemcpyAsync(staging, bytes + row0 * w->m.row_bytes, raw, cudaMemcpyHostToDevice,
+                          c->stream);
+    if (e == cudaSuccess) e = launch_repack(staging, w->m, w->buf, c->stream);
+    if (e == cudaSuccess)
+      e = cudaMemsetAsync(w->buf + rows * w->m.pitch, 0, w->bytes - rows * w->m.pitch, c->stream);
+    if (staging) cudaFreeAsync(staging, c->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+  }
+  if (e != cudaSuccess) {
+    cudaFree(w->buf);
+    delete w;
+    return gpu_fail(c, e, "weight upload");
+  }
+  *out = w;
+  return VTQ_OK;
+}
+
+// Shared body of the host-slice entry points: validate like the reference,
+// upload, run, free.
+vtq_status host_linear(vtq_ctx* c, int dtype, const float* x, const uint8_t* w, size_t wlen,
+                       float* y, size_t batch, size_t in, size_t out, uint32_t flags) {
+  if (!c || (!x && batch * in) || (!w && wlen) || (!y && batch * out))
+    return fail(c, VTQ_ERR_INVALID_ARG, "null argument");
+  if (out == 0 || batch == 0) return VTQ_OK;
+  vtq_weight* wt = nullptr;
+  if (vtq_status s = upload(c, dtype, w, (int64_t)in, 0, (int64_t)out, &wt)) return s;
+  const vtq_status s = linear_host(c, wt->m, x, y, (int64_t)batch, flags | VTQ_PTR_HOST);
+  cudaFree(wt->buf);
+  delete wt;
+  return s;
+}
+
+// Reference validation for the integer k-quant linears (quant.rs:944-949, :1068-1073).
+vtq_status check_kquant(vtq_ctx* c, const char* fn, int bytes_per_sb, size_t wlen, size_t in,
+                        size_t out) {
+  if (in % 256) return fail(c, VTQ_ERR_INTERNAL, std::string(fn) + ": in_feat not a multiple of 256");
+  if (wlen < out * (in / 256) * bytes_per_sb)
+    return fail(c, VTQ_ERR_INTERNAL, std::string(fn) + ": weight shape mismatch");
+  return VTQ_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+vtq_status vtq_init(int device, vtq_ctx** out) {
+  if (!out) return VTQ_ERR_INVALID_ARG;
+  *out = nullptr;
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess || device < 0 || device >= n) return VTQ_ERR_GPU;
+  auto* c = new vtq_ctx();
+  c->device = device;
+  cudaError_t e = cudaSetDevice(device);
+  if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&c->own, cudaStreamNonBlocking);
+  if (e != cudaSuccess) {
+    delete c;
+    return VTQ_ERR_GPU;
+  }
+  c->stream = c->own;
+  if (ensure_io(c, kStatusBytes + 64 * 1024) != VTQ_OK) {
+    cudaStreamDestroy(c->own);
+    delete c;
+    return VTQ_ERR_OOM;
+  }
+  *out = c;
+  return VTQ_OK;
+}
+
+vtq_status vtq_destroy(vtq_ctx* c) {
+  if (!c) return VTQ_ERR_INVALID_ARG;
+  cudaSetDevice(c->device);
+  cudaStreamSynchronize(c->stream);
+  if (c->io) cudaFree(c->io);
+  if (c->own) cudaStreamDestroy(c->own);
+  delete c;
+  return VTQ_OK;
+}
+
+const char* vtq_last_error(const vtq_ctx* c) { return c ? c->err.c_str() : "null context"; }
+
+vtq_status vtq_set_stream(vtq_ctx* c, void* s) {
+  if (!c) return VTQ_ERR_INVALID_ARG;
+  c->stream = s ? static_cast<cudaStream_t>(s) : c->own;
+  return VTQ_OK;
+}
+
+vtq_status vtq_synchronize(vtq_ctx* c) {
+  if (!c) return VTQ_ERR_INVALID_ARG;
+  VTQ_CUDA(c, cudaSetDevice(c->device));
+  VTQ_CUDA(c, cudaStreamSynchronize(c->stream));
+  return VTQ_OK;
+}
+
+vtq_status vtq_weight_upload(vtq_ctx* c, int32_t dtype, const uint8_t* bytes, size_t nbytes,
+                             int64_t in_feat, int64_t out_feat, int64_t row_begin, int64_t row_end,
+                             vtq_weight** out) {
+  if (!c || !out || (!bytes && nbytes)) return fail(c, VTQ_ERR_INVALID_ARG, "null argument");
+  *out = nullptr;
+  if (!dtype_supported(dtype))
+    return fail(c, VTQ_ERR_NOT_IMPLEMENTED,
+                "vtq_weight_upload: not implemented (weight dtype not Q4_0 / Q4_K / Q5_0 / Q6_K / "
+                "Q8_0 / F32)");
+  if (in_feat <= 0 || out_feat < 0) return fail(c, VTQ_ERR_INTERNAL, "vtq_weight_upload: bad shape");
+  const int64_t rb = packed_row_bytes(dtype, in_feat);
+  if (rb < 0)
+    return fail(c, VTQ_ERR_INTERNAL, "vtq_weight_upload: in_feat not a multiple of the block size");
+  if (row_end < 0) row_end = out_feat;
+  if (row_begin < 0 || row_begin > row_end || row_end > out_feat)
+    return fail(c, VTQ_ERR_INTERNAL, "vtq_weight_upload: row range outside [0, out_feat]");
+  if ((int64_t)nbytes < out_feat * rb)
+    return fail(c, VTQ_ERR_INTERNAL, "vtq_weight_upload: weight blob too small");
+  VTQ_CUDA(c, cudaSetDevice(c->device));
+  return upload(c, dtype, bytes, in_feat, row_begin, row_end - row_begin, out);
+}
+
+vtq_status vtq_weight_free(vtq_weight* w) {
+  if (!w) return VTQ_ERR_INVALID_ARG;
+  cudaSetDevice(w->ctx->device);
+  cudaStreamSynchronize(w->ctx->stream);
+  cudaFree(w->buf);
+  delete w;
+  return VTQ_OK;
+}
+
+vtq_status vtq_weight_info(const vtq_weight* w, int32_t* dtype, int64_t* in_feat, int64_t* rows,
+                           size_t* device_bytes) {
+  if (!w) return VTQ_ERR_INVALID_ARG;
+  if (dtype) *dtype = w->m.dtype;
+  if (in_feat) *in_feat = w->m.in_feat;
+  if (rows) *rows = w->m.out_feat;
+  if (device_bytes) *device_bytes = w->bytes;
+  return VTQ_OK;
+}
+
+vtq_status vtq_linear(vtq_ctx* c, const vtq_weight* w, const float* x, float* y, int64_t batch,
+                      uint32_t flags) {
+  if (!c || !w || !x || !y) return fail(c, VTQ_ERR_INVALID_ARG, "null argument");
+  if (batch < 0) return fail(c, VTQ_ERR_INTERNAL, "vtq_linear: negative batch");
+  if (batch == 0 || w->m.out_feat == 0) return VTQ_OK;
+  VTQ_CUDA(c, cudaSetDevice(c->device));
+  if (flags & VTQ_PTR_HOST) return linear_host(c, w->m, x, y, batch, flags);
+  if (vtq_status s = check_kernel_limits(c, w->m, flags)) return s;
+  VTQ_CUDA(c, run_linear(w->m, x, w->m.in_feat, y, w->m.out_feat, batch, flags,
+                         reinterpret_cast<unsigned*>(c->io), c->stream));
+  return VTQ_OK;
+}
+
+vtq_status vtq_linear_dispatch(vtq_ctx* c, int32_t dtype, const float* x, const uint8_t* w,
+                               size_t wlen, size_t in, size_t out, float* y, uint32_t flags) {
+  if (!c) return VTQ_ERR_INVALID_ARG;
+  switch (dtype) {
+    case T_Q4_0:
+      return vtq_linear_q4_0(c, x, w, wlen, y, 1, in, out);
+    case T_F32:
+      if (wlen != out * in * 4)
+        return fail(c, VTQ_ERR_INTERNAL, "linear_dispatch F32: weight size mismatch");
+      return host_linear(c, dtype, x, w, wlen, y, 1, in, out, flags);
+    case T_Q4_K:
+      if (flags & VTQ_Q4K_FLOAT) return vtq_linear_q4_k_fused(c, x, w, wlen, y, 1, in, out);
+      return vtq_linear_q4_k_integer(c, x, w, wlen, y, 1, in, out);
+    case T_Q6_K:
+      return vtq_linear_q6_k_integer(c, x, w, wlen, y, 1, in, out);
+    case T_Q8_0:
+    case T_Q5_0: {
+      const char* nm = dtype == T_Q8_0 ? "Q8_0" : "Q5_0";
+      if (in % 32)
+        return fail(c, VTQ_ERR_INTERNAL, std::string(nm) + ": in_feat must be a multiple of 32");
+      if (wlen < out * (in / 32) * (dtype == T_Q8_0 ? 34 : 22))
+        return fail(c, VTQ_ERR_INTERNAL, std::string("linear_dispatch ") + nm + ": weight blob too small");
+      return host_linear(c, dtype, x, w, wlen, y, 1, in, out, flags);
+    }
+    default:
+      return fail(c, VTQ_ERR_NOT_IMPLEMENTED,
+                  "forward_quantized::linear_dispatch: not implemented (weight dtype not Q4_0 / "
+                  "Q4_K / Q5_0 / Q6_K / Q8_0 / F32)");
+  }
+}
+
+vtq_status vtq_linear_q4_k_integer(vtq_ctx* c, const float* x, const uint8_t* w, size_t wlen,
+                                   float* y, size_t batch, size_t in, size_t out) {
+  if (!c) return VTQ_ERR_INVALID_ARG;
+  if (vtq_status s = check_kquant(c, "linear_q4_k_integer", 144, wlen, in, out)) return s;
+  return host_linear(c, T_Q4_K, x, w, wlen, y, batch, in, out, 0);
+}
+
+vtq_status vtq_linear_q6_k_integer(vtq_ctx* c, const float* x, const uint8_t* w, size_t wlen,
+                                   float* y, size_t batch, size_t in, size_t out) {
+  if (!c) return VTQ_ERR_INVALID_ARG;
+  if (vtq_status s = check_kquant(c, "linear_q6_k_integer", 210, wlen, in, out)) return s;
+  return host_linear(c, T_Q6_K, x, w, wlen, y, batch, in, out, 0);
+}
+
+vtq_status vtq_linear_q4_k_fused(vtq_ctx* c, const float* x, const uint8_t* w, size_t wlen,
+                                 float* y, size_t batch, size_t in, size_t out) {
+  if (!c) return VTQ_ERR_INVALID_ARG;
+  if (in % 256) return fail(c, VTQ_ERR_INTERNAL, "linear_q4_k_fused: in_feat not a multiple of 256");
+  if (wlen < out * (in / 256) * 144)
+    return fail(c, VTQ_ERR_INTERNAL, "linear_q4_k_fused: weight shape mismatch");
+  return host_linear(c, T_Q4_K, x, w, wlen, y, batch, in, out, VTQ_Q4K_FLOAT);
+}
+
+vtq_status vtq_linear_q4_0(vtq_ctx* c, const float* x, const uint8_t* w, size_t wlen, float* y,
+                           size_t batch, size_t in, size_t out) {
+  if (!c) return VTQ_ERR_INVALID_ARG;
+  if (in % 32) return fail(c, VTQ_ERR_INTERNAL, "linear_q4_0: in_feat must be multiple of 32");
+  if (wlen != out * (in / 32) * 18)
+    return fail(c, VTQ_ERR_INTERNAL, "linear_q4_0: weight blob length mismatch");
+  return host_linear(c, T_Q4_0, x, w, wlen, y, batch, in, out, 0);
+}
+
+int64_t vtq_device_layout_bytes(int32_t dtype, int64_t in_feat, int64_t rows) {
+  const int64_t p = device_pitch(dtype, in_feat);
+  if (p < 0 || rows < 0) return -1;
+  return p * rows + 16;
+}
+
+vtq_status vtq_device_repack(int32_t dtype, int64_t in_feat, int64_t rows, const uint8_t* src_dev,
+                             uint8_t* dst_dev, void* s) {
+  if (!dtype_supported(dtype)) return VTQ_ERR_NOT_IMPLEMENTED;
+  const int64_t rb = packed_row_bytes(dtype, in_feat);
+  if (rb < 0 || rows < 0) return VTQ_ERR_INTERNAL;
+  if ((!src_dev || !dst_dev) && rows) return VTQ_ERR_INVALID_ARG;
+  DevMatrix m{dtype, in_feat, rows, rb, device_pitch(dtype, in_feat), dst_dev};
+  cudaStream_t st = static_cast<cudaStream_t>(s);
+  if (launch_repack(src_dev, m, dst_dev, st) != cudaSuccess) return VTQ_ERR_GPU;
+  if (cudaMemsetAsync(dst_dev + rows * m.pitch, 0, 16, st) != cudaSuccess) return VTQ_ERR_GPU;
+  return VTQ_OK;
+}
+
+vtq_status vtq_linear_device(int32_t dtype, const uint8_t* w_dev, int64_t in_feat, int64_t rows,
+                             const float* x_dev, int64_t ldx, float* y_dev, int64_t ldy,
+                             int64_t batch, uint32_t flags, uint32_t* status_dev, void* s) {
+  if (!dtype_supported(dtype)) return VTQ_ERR_NOT_IMPLEMENTED;
+  const int64_t rb = packed_row_bytes(dtype, in_feat);
+  if (rb < 0 || rows < 0 || batch < 0 || ldx < in_feat || ldy < rows) return VTQ_ERR_INTERNAL;
+  if (batch == 0 || rows == 0) return VTQ_OK;
+  if (!w_dev || !x_dev || !y_dev) return VTQ_ERR_INVALID_ARG;
+  if (in_feat > 32768) return VTQ_ERR_NOT_IMPLEMENTED;
+  if (reinterpret_cast<uintptr_t>(w_dev) & 15u) return VTQ_ERR_INVALID_ARG;
+  DevMatrix m{dtype, in_feat, rows, rb, device_pitch(dtype, in_feat), w_dev};
+  if (run_linear(m, x_dev, ldx, y_dev, ldy, batch, flags, status_dev, static_cast<cudaStream_t>(s)) !=
+      cudaSuccess)
+    return VTQ_ERR_GPU;
+  return VTQ_OK;
+}
+
+}  // extern "C"

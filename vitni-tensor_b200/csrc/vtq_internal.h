@@ -1,0 +1,46 @@
+// vtq_internal.h -- launchers shared between the kernel files and the C ABI.
+#pragma once
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace vtq {
+
+// GGML type tags (vitni-tensor src/model/gguf.rs:127-139).
+enum GgmlType : int { T_F32 = 0, T_F16 = 1, T_Q4_0 = 2, T_Q5_0 = 6, T_Q8_0 = 8, T_Q4_K = 12, T_Q6_K = 14 };
+
+// Device layout of a weight matrix. Rows are re-pitched to a multiple of 16
+// bytes so every row starts on a bulk-copy boundary. Q6_K superblocks are
+// additionally regrouped in runs of 8 (see repack.cu) so that each field of
+// each superblock is 16-byte aligned in shared memory. All other formats keep
+// their GGUF byte order within a row.
+struct DevMatrix {
+  int dtype;
+  int64_t in_feat, out_feat;  // n, R
+  int64_t row_bytes;          // packed GGUF bytes per row
+  int64_t pitch;              // device bytes per row (multiple of 16)
+  const uint8_t* data;        // device pointer, 256-byte aligned, + 16 B tail pad
+};
+
+int64_t packed_row_bytes(int dtype, int64_t in_feat);  // -1 if in_feat invalid
+int64_t device_pitch(int dtype, int64_t in_feat);
+
+// Raw GGUF rows (host or device bytes already on device in `staging`) to the
+// device layout. `staging` holds out_feat*row_bytes packed bytes.
+cudaError_t launch_repack(const uint8_t* staging, const DevMatrix& m, uint8_t* dst,
+                          cudaStream_t st);
+
+// Integer k-quant matvec (Q4_K / Q6_K against int8-quantised activations):
+// y[b, r] for r in [0, R), b in [0, batch). x row stride ldx, y row stride ldy.
+cudaError_t launch_kq_matvec(const DevMatrix& m, const float* x, int64_t ldx, int64_t batch,
+                             float* y, int64_t ldy, unsigned* status, cudaStream_t st);
+
+// Canonical fp32 matvec (8 pinned lanes, 8192-element chunks, fixed trees)
+// for Q8_0 / Q5_0 / Q4_0 / F32 rows and the float-fused Q4_K mode.
+cudaError_t launch_canon_matvec(const DevMatrix& m, const float* x, int64_t ldx, int64_t batch,
+                                float* y, int64_t ldy, unsigned* status, cudaStream_t st);
+
+int num_sms();
+int max_smem_optin();
+
+}  // namespace vtq

@@ -1,0 +1,265 @@
+"""vtq -- Python host binding of the B200 k-quant linear backend (C ABI: include/vtq.h).
+
+Mirrors vitni-tensor's quantized-linear interface: the same function names,
+argument meaning (x [batch][in_feat] f32, row-major weight bytes, y_out
+[batch][out_feat]) and error behaviour (``Internal`` for shape/length checks,
+``NotImplemented`` for unsupported dtypes), as in src/ops/quant.rs and
+src/model/forward_quantized.rs:663-785 of the reference.
+
+All arithmetic runs in libvtq.so's sm_100a kernels. There is no CPU fallback:
+importing works without a GPU, but any compute call raises if the library or a
+device is missing.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+import numpy as np
+
+from .formats import (F32, Q4_0, Q5_0, Q8_0, Q4_K, Q6_K, QuantTensor, row_bytes)  # noqa: F401
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libvtq.so")
+
+PTR_HOST = 1
+Q4K_FLOAT = 2
+
+# Status codes (include/vtq.h).
+OK, ERR_INTERNAL, ERR_NOT_IMPLEMENTED, ERR_GPU, ERR_OOM, ERR_TIMEOUT, ERR_INVALID_ARG = range(7)
+ERR_MALFORMED, ERR_TRUNCATED = 7, 8
+
+# Every symbol include/vtq.h declares.
+EXPORTS = (
+    "vtq_init", "vtq_destroy", "vtq_last_error", "vtq_set_stream", "vtq_synchronize",
+    "vtq_weight_upload", "vtq_weight_free", "vtq_weight_info", "vtq_linear",
+    "vtq_linear_dispatch", "vtq_linear_q4_k_integer", "vtq_linear_q6_k_integer",
+    "vtq_linear_q4_k_fused", "vtq_linear_q4_0", "vtq_device_layout_bytes",
+    "vtq_device_repack", "vtq_linear_device",
+)
+
+
+class Error(Exception):
+    """Base of the reference's error enum (src/error.rs:7-63)."""
+
+    status = -1
+
+
+class Internal(Error):
+    status = ERR_INTERNAL
+
+
+class NotImplementedOp(Error):
+    status = ERR_NOT_IMPLEMENTED
+
+
+class GpuError(Error):
+    status = ERR_GPU
+
+
+class OutOfMemory(Error):
+    status = ERR_OOM
+
+
+class Timeout(Error):
+    status = ERR_TIMEOUT
+
+
+class InvalidArg(Error):
+    status = ERR_INVALID_ARG
+
+
+class Malformed(Error):
+    status = ERR_MALFORMED
+
+
+class Truncated(Error):
+    status = ERR_TRUNCATED
+
+
+_ERRORS = {c.status: c for c in (Internal, NotImplementedOp, GpuError, OutOfMemory, Timeout,
+                                 InvalidArg, Malformed, Truncated)}
+
+_lib = None
+
+
+def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
+    """Load libvtq.so (raises OSError if it has not been built)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(path):
+        raise OSError(f"libvtq.so not built at {path}: run vitni-tensor_b200/build.py")
+    lib = ctypes.CDLL(path)
+    c_p, c_i32, c_i64, c_sz, c_u32 = (ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64,
+                                       ctypes.c_size_t, ctypes.c_uint32)
+    sig = {
+        "vtq_init": (c_i32, [ctypes.c_int, ctypes.POINTER(c_p)]),
+        "vtq_destroy": (c_i32, [c_p]),
+        "vtq_last_error": (ctypes.c_char_p, [c_p]),
+        "vtq_set_stream": (c_i32, [c_p, c_p]),
+        "vtq_synchronize": (c_i32, [c_p]),
+        "vtq_weight_upload": (c_i32, [c_p, c_i32, c_p, c_sz, c_i64, c_i64, c_i64, c_i64,
+                                      ctypes.POINTER(c_p)]),
+        "vtq_weight_free": (c_i32, [c_p]),
+        "vtq_weight_info": (c_i32, [c_p, ctypes.POINTER(c_i32), ctypes.POINTER(c_i64),
+                                    ctypes.POINTER(c_i64), ctypes.POINTER(c_sz)]),
+        "vtq_linear": (c_i32, [c_p, c_p, c_p, c_p, c_i64, c_u32]),
+        "vtq_linear_dispatch": (c_i32, [c_p, c_i32, c_p, c_p, c_sz, c_sz, c_sz, c_p, c_u32]),
+        "vtq_linear_q4_k_integer": (c_i32, [c_p, c_p, c_p, c_sz, c_p, c_sz, c_sz, c_sz]),
+        "vtq_linear_q6_k_integer": (c_i32, [c_p, c_p, c_p, c_sz, c_p, c_sz, c_sz, c_sz]),
+        "vtq_linear_q4_k_fused": (c_i32, [c_p, c_p, c_p, c_sz, c_p, c_sz, c_sz, c_sz]),
+        "vtq_linear_q4_0": (c_i32, [c_p, c_p, c_p, c_sz, c_p, c_sz, c_sz, c_sz]),
+        "vtq_device_layout_bytes": (c_i64, [c_i32, c_i64, c_i64]),
+        "vtq_device_repack": (c_i32, [c_i32, c_i64, c_i64, c_p, c_p, c_p]),
+        "vtq_linear_device": (c_i32, [c_i32, c_p, c_i64, c_i64, c_p, c_i64, c_p, c_i64, c_i64,
+                                      c_u32, c_p, c_p]),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = lib
+    return lib
+
+
+def _ptr(a: np.ndarray) -> int:
+    return a.ctypes.data
+
+
+class Weight:
+    """A device-resident weight matrix (rows [row_begin, row_end) of W)."""
+
+    def __init__(self, ctx: "Context", handle: int, dtype: int, in_feat: int, rows: int,
+                 row_begin: int):
+        self.ctx, self.handle, self.dtype = ctx, handle, dtype
+        self.in_feat, self.rows, self.row_begin = in_feat, rows, row_begin
+
+    def device_bytes(self) -> int:
+        sz = ctypes.c_size_t()
+        self.ctx._check(self.ctx.lib.vtq_weight_info(self.handle, None, None, None,
+                                                      ctypes.byref(sz)))
+        return sz.value
+
+    def free(self):
+        if self.handle:
+            self.ctx.lib.vtq_weight_free(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+class Context:
+    """One CUDA device + stream (vtq_init)."""
+
+    def __init__(self, device: int = 0):
+        self.lib = load_library()
+        h = ctypes.c_void_p()
+        st = self.lib.vtq_init(device, ctypes.byref(h))
+        if st != OK:
+            raise _ERRORS.get(st, Error)(f"vtq_init({device}) failed with status {st}")
+        self.handle = h.value
+        self.device = device
+
+    def _check(self, st: int):
+        if st != OK:
+            msg = self.lib.vtq_last_error(self.handle).decode()
+            raise _ERRORS.get(st, Error)(msg)
+
+    def close(self):
+        if getattr(self, "handle", None):
+            self.lib.vtq_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def set_stream(self, stream_ptr: int | None):
+        self._check(self.lib.vtq_set_stream(self.handle, stream_ptr))
+
+    def synchronize(self):
+        self._check(self.lib.vtq_synchronize(self.handle))
+
+    # -- resident weights -------------------------------------------------
+    def upload(self, dtype: int, data, in_feat: int, out_feat: int, row_begin: int = 0,
+               row_end: int = -1) -> Weight:
+        buf = np.frombuffer(bytes(data), np.uint8) if not isinstance(data, np.ndarray) else \
+            np.ascontiguousarray(data).view(np.uint8).reshape(-1)
+        h = ctypes.c_void_p()
+        self._check(self.lib.vtq_weight_upload(self.handle, dtype, _ptr(buf), buf.nbytes, in_feat,
+                                               out_feat, row_begin, row_end, ctypes.byref(h)))
+        re = out_feat if row_end < 0 else row_end
+        return Weight(self, h.value, dtype, in_feat, re - row_begin, row_begin)
+
+    def linear(self, w: Weight, x: np.ndarray, batch: int = 1, q4k_float: bool = False
+               ) -> np.ndarray:
+        """y = W x for host arrays (copies in/out inside the call)."""
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        if x.size != batch * w.in_feat:
+            raise Internal("vtq_linear: x shape mismatch")
+        y = np.empty(batch * w.rows, np.float32)
+        flags = PTR_HOST | (Q4K_FLOAT if q4k_float else 0)
+        self._check(self.lib.vtq_linear(self.handle, w.handle, _ptr(x), _ptr(y), batch, flags))
+        return y
+
+    def linear_ptr(self, w: Weight, x_ptr: int, y_ptr: int, batch: int = 1, host: bool = False,
+                   q4k_float: bool = False):
+        """vtq_linear on raw pointers (device pointers unless host=True)."""
+        flags = (PTR_HOST if host else 0) | (Q4K_FLOAT if q4k_float else 0)
+        self._check(self.lib.vtq_linear(self.handle, w.handle, x_ptr, y_ptr, batch, flags))
+
+
+# -- reference-signature functions (host slices) ---------------------------------
+
+def _as_f32(x) -> np.ndarray:
+    return np.ascontiguousarray(x, dtype=np.float32)
+
+
+def _as_u8(w) -> np.ndarray:
+    if isinstance(w, np.ndarray):
+        return np.ascontiguousarray(w).view(np.uint8).reshape(-1)
+    return np.frombuffer(bytes(w), np.uint8)
+
+
+def _op(name: str):
+    def fn(ctx: Context, x, w, y_out: np.ndarray, batch: int, in_feat: int, out_feat: int):
+        xa, wa = _as_f32(x), _as_u8(w)
+        if y_out.dtype != np.float32 or not y_out.flags.c_contiguous:
+            raise Internal(f"{name}: y_out must be contiguous float32")
+        if xa.size < batch * in_feat or y_out.size < batch * out_feat:
+            raise Internal(f"{name}: x/y size mismatch")
+        ctx._check(getattr(ctx.lib, "vtq_" + name)(ctx.handle, _ptr(xa), _ptr(wa), wa.nbytes,
+                                                   _ptr(y_out), batch, in_feat, out_feat))
+    fn.__name__ = name
+    fn.__doc__ = f"Bit-identical GPU replacement of the reference's `{name}` (host slices)."
+    return fn
+
+
+linear_q4_k_integer = _op("linear_q4_k_integer")
+linear_q6_k_integer = _op("linear_q6_k_integer")
+linear_q4_k_fused = _op("linear_q4_k_fused")
+linear_q4_0 = _op("linear_q4_0")
+
+
+def linear_dispatch(ctx: Context, x, w: QuantTensor, in_feat: int, out_feat: int,
+                    q4k_float: bool = False) -> np.ndarray:
+    """linear_dispatch (src/model/forward_quantized.rs:663-785): batch 1, returns y."""
+    xa, wa = _as_f32(x), _as_u8(w.bytes)
+    if xa.size < in_feat:
+        raise Internal("linear_dispatch: x shorter than in_feat")
+    y = np.zeros(out_feat, np.float32)
+    ctx._check(ctx.lib.vtq_linear_dispatch(ctx.handle, w.dtype, _ptr(xa), _ptr(wa), wa.nbytes,
+                                           in_feat, out_feat, _ptr(y),
+                                           Q4K_FLOAT if q4k_float else 0))
+    return y
+
+
+def device_layout_bytes(dtype: int, in_feat: int, rows: int) -> int:
+    return load_library().vtq_device_layout_bytes(dtype, in_feat, rows)
