@@ -5,38 +5,47 @@
 //   linear_q6_k_integer(_parallel)  src/ops/quant.rs:1060-1146
 // y[b, r] = fixed_tree_s( blockdot(W[r, s], quantize_block_q8(x[b, 256s..])) ).
 //
-// Design (one persistent CTA per SM, 8 warps):
+// Design (one persistent CTA per SM: 8 consumer warps + 1 TMA producer warp):
 //  * Each CTA owns a contiguous range of output rows, i.e. one contiguous byte
-//    range of the weight matrix in HBM. Thread 0 streams it into a shared-
-//    memory ring with TMA bulk copies (cp.async.bulk + mbarrier complete_tx,
-//    L2 evict-first) -- stages are whole rows, the ring is as deep as shared
-//    memory allows, so small matrices are requested in full at kernel entry.
-//  * While the first stages are in flight, every CTA quantises the activation
-//    rows into shared memory (quantize_block_q8, quant.rs:750-771, restated
-//    with __fdiv_rn/__fmul_rn/__fadd_rn and cvt.rzi; identical bits in every
-//    CTA, so the reference's once-per-call quantisation is reproduced).
-//  * 4 lanes cooperate on one superblock: each unpacks its quarter of the
-//    packed quants with shifts/masks and forms exact int32 dots with dp4a.
-//    Integer sums are exact, so the lane split and shuffle order are free.
-//    Only the per-superblock fp combine (quant.rs:897 / :1056) and the
-//    cross-superblock fixed_tree (quant.rs:462) are order-pinned; both run
-//    with explicit round-to-nearest intrinsics (no FMA contraction) in the
-//    reference's order.
-//  * When a stage's rows are complete, one warp per (row, batch) reduces the
-//    S superblock partials with a stride-doubling shuffle tree whose pairing
-//    is identical to the reference's level-wise fixed_tree.
+//    range of the weight matrix in HBM. The producer warp streams it into a
+//    shared-memory ring of whole-row stages with TMA bulk copies
+//    (cp.async.bulk, mbarrier complete_tx, L2 evict-first). full/empty
+//    mbarrier pairs decouple it from the consumers; small matrices are
+//    requested in full at kernel entry.
+//  * Meanwhile the consumer warps quantise the activation rows into shared
+//    memory (quantize_block_q8, quant.rs:750-771, restated with __fdiv_rn /
+//    __fmul_rn / __fadd_rn and cvt.rzi -- the same bits in every CTA, so the
+//    reference's once-per-call quantisation is reproduced). Activation blocks
+//    are padded to 272 B so that lanes reading different superblocks at the
+//    same offset hit different shared-memory banks.
+//  * One lane owns one whole superblock of one row: it unpacks the quants
+//    with masks/shifts and forms exact int32 dots with dp4a, so scale decoding
+//    happens once per superblock and no cross-lane integer reduction is
+//    needed. A row's S superblocks sit on S consecutive lanes (a warp holds
+//    32/S rows when S <= 16); S > 32 puts up to 4 superblocks on a lane.
+//  * The per-superblock fp combine (quant.rs:897 / :1056) and the
+//    cross-superblock fixed_tree (quant.rs:462) are the only order-pinned
+//    steps; both use explicit round-to-nearest intrinsics (no contraction).
+//    The tree is a stride-doubling shuffle tree over the row's lanes whose
+//    pairing is identical to the reference's level-wise loop.
 #include "vtq_device.cuh"
 #include "vtq_internal.h"
+#include <cuda_fp16.h>
 
 namespace vtq {
 namespace {
 
-constexpr int KQ_WARPS = 8;
-constexpr int KQ_THREADS = KQ_WARPS * 32;
-constexpr int KQ_BMAX = 8;      // activation rows per launch
-constexpr int KQ_NST_MAX = 8;   // ring depth
-constexpr int KQ_SMAX = 128;    // superblocks per row (in_feat <= 32768)
+constexpr int KQ_NST_MAX = 16;                   // ring depth
+constexpr int KQ_SMAX = 128;                     // superblocks per row (in_feat <= 32768)
+constexpr int XQ_STRIDE = 272;                   // padded bytes per quantised activation block
 constexpr uint32_t FULL = 0xffffffffu;
+
+#ifdef VTQ_TRACE
+__device__ unsigned long long g_kq_trace[1024][8];
+#define KQ_TRACE(slot) g_kq_trace[blockIdx.x][slot] = (slot == 0 ? globaltimer() : clock64())
+#else
+#define KQ_TRACE(slot) (void)0
+#endif
 
 struct KqParams {
   const float* x;
@@ -45,34 +54,38 @@ struct KqParams {
   const uint8_t* W;
   int64_t pitch;
   int R;
+  int rows_base, rows_rem;  // CTA b owns rows_base (+1 if b < rows_rem) rows
   float* y;
   int64_t ldy;
-  int rps;                 // rows per stage
-  int nst;                 // ring depth
-  uint32_t stage_bytes;    // rps * pitch
-  uint32_t off_xd, off_bsum, off_part, off_xq, off_stage;
+  int rps;                  // rows per stage (multiple of rows per warp pass)
+  int nst;                  // ring depth
+  uint32_t stage_bytes;     // rps * pitch
+  int lpr;                  // lanes per row segment (power of two, <= 32)
+  int x_smem;               // x rows fetched by TMA into off_xf
+  uint32_t off_xd, off_bsum, off_xq, off_xf, off_stage;
   unsigned* status;
 };
 
 // quantize_block_q8 for every (batch row, superblock): one warp per block,
-// 8 contiguous elements per lane. NB = 8 (sums per 32, Q4_K's bsums) or 16
-// (sums per 16, used for Q6_K's -32 offset).
-template <int NB>
-__device__ __forceinline__ void quantize_x(const KqParams& p, float* xd, int* bsum, int8_t* xq) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+// 8 contiguous elements per lane. NB = 8 (sums per 32: Q4_K's bsums) or 16
+// (sums per 16: the Q6_K -32 offset term). `xs` is the activation source:
+// the TMA-staged rows in shared memory (row stride n) or global x (ldx).
+template <int NB, int CW>
+__device__ __forceinline__ void quantize_x(const KqParams& p, const float* xs, int64_t lds,
+                                           int warp, int lane, float* xd, int* bsum, int8_t* xq) {
   const int nblk = p.batch * p.S;
-  for (int u = warp; u < nblk; u += KQ_WARPS) {
+  for (int u = warp; u < nblk; u += CW) {
     const int b = u / p.S, s = u - b * p.S;
-    const float* src = p.x + (int64_t)b * p.ldx + (int64_t)s * 256 + lane * 8;
+    const float* src = xs + (int64_t)b * lds + s * 256 + lane * 8;
     float v[8];
     if ((reinterpret_cast<uintptr_t>(src) & 15u) == 0) {
-      const float4 a = __ldg(reinterpret_cast<const float4*>(src));
-      const float4 c = __ldg(reinterpret_cast<const float4*>(src) + 1);
+      const float4 a = *reinterpret_cast<const float4*>(src);
+      const float4 c = *(reinterpret_cast<const float4*>(src) + 1);
       v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
       v[4] = c.x; v[5] = c.y; v[6] = c.z; v[7] = c.w;
     } else {
 #pragma unroll
-      for (int i = 0; i < 8; i++) v[i] = __ldg(src + i);
+      for (int i = 0; i < 8; i++) v[i] = src[i];
     }
     // amax = max over non-NaN |v|, starting at +0.0 (quant.rs:752-758).
     uint32_t am = 0;
@@ -101,241 +114,409 @@ __device__ __forceinline__ void quantize_x(const KqParams& p, float* xd, int* bs
     } else {
       if ((lane & 1) == 0) bsum[blk * 16 + (lane >> 1)] = s16;
     }
-    *reinterpret_cast<uint2*>(xq + (int64_t)b * p.n + s * 256 + lane * 8) = make_uint2(w0, w1);
+    *reinterpret_cast<uint2*>(xq + blk * XQ_STRIDE + lane * 8) = make_uint2(w0, w1);
     if (lane == 0) xd[blk] = d;
   }
 }
 
-// Q4_K: scales for sub-blocks 2h, 2h+1 (get_scale_min_k4, quant.rs:268-276).
-__device__ __forceinline__ void q4k_scales(uint32_t w0, uint32_t w1, uint32_t w2, int h, int& sc0,
-                                           int& sc1, int& m0, int& m1) {
-  const int sh = (h & 1) * 16;
-  const uint32_t a = w0 >> sh, m = w1 >> sh, hi = w2 >> sh;
-  if (h < 2) {
-    sc0 = a & 63; sc1 = (a >> 8) & 63;
-    m0 = m & 63;  m1 = (m >> 8) & 63;
-  } else {
-    sc0 = (hi & 15) | (((a >> 6) & 3) << 4);
-    sc1 = ((hi >> 8) & 15) | (((a >> 14) & 3) << 4);
-    m0 = ((hi >> 4) & 15) | (((m >> 6) & 3) << 4);
-    m1 = ((hi >> 12) & 15) | (((m >> 14) & 3) << 4);
-  }
+// dp4a, signed x signed bytes.
+__device__ __forceinline__ int dot_ss(uint4 q, int4 x) {
+  int a = __dp4a((int)q.x, x.x, 0);
+  int b = __dp4a((int)q.y, x.y, 0);
+  a = __dp4a((int)q.z, x.z, a);
+  b = __dp4a((int)q.w, x.w, b);
+  return a + b;
 }
 
-// One Q4_K superblock (raw GGUF layout, 144 B) against one activation block.
-// Lane quarter h owns qs[32h..32h+32) = elements 64h..64h+64.
-// Returns this lane's partial float (valid in the h == 0 lane only).
-__device__ __forceinline__ void q4k_unit(const uint8_t* sb, int h, const KqParams& p,
-                                         const int8_t* xq, const float* xd, const int* bsum,
-                                         int s, float* out, int out_stride, bool valid) {
-  const uint4 qa = *reinterpret_cast<const uint4*>(sb + 16 + 32 * h);
-  const uint4 qb = *reinterpret_cast<const uint4*>(sb + 32 + 32 * h);
-  const uint32_t qw[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-  const uint32_t sw0 = *reinterpret_cast<const uint32_t*>(sb + 4);
-  const uint32_t sw1 = *reinterpret_cast<const uint32_t*>(sb + 8);
-  const uint32_t sw2 = *reinterpret_cast<const uint32_t*>(sb + 12);
-  const uint32_t dw = *reinterpret_cast<const uint32_t*>(sb);
-  int sc0, sc1, m0, m1;
-  q4k_scales(sw0, sw1, sw2, h, sc0, sc1, m0, m1);
-  uint32_t lo[8], hi[8];
+// dp4a, unsigned bytes of q x signed bytes of x.
+__device__ __forceinline__ int dp4a_us(uint32_t a, int b, int c) {
+  int d;
+  asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+__device__ __forceinline__ int dot_us(uint4 q, int4 x) {
+  int a = dp4a_us(q.x, x.x, 0);
+  int b = dp4a_us(q.y, x.y, 0);
+  a = dp4a_us(q.z, x.z, a);
+  b = dp4a_us(q.w, x.w, b);
+  return a + b;
+}
+
+__device__ __forceinline__ uint4 mask4(uint4 v, uint32_t m) {
+  return make_uint4(v.x & m, v.y & m, v.z & m, v.w & m);
+}
+
+__device__ __forceinline__ int4 lds_i4(const int8_t* p) { return *reinterpret_cast<const int4*>(p); }
+__device__ __forceinline__ uint4 lds_u4(const uint8_t* p) {
+  return *reinterpret_cast<const uint4*>(p);
+}
+
+// binary16 -> binary32 through the hardware convert: exact for every finite
+// value and infinity (subnormal halves are normal floats). Only a NaN's
+// payload may differ from the reference's bit-level decode; NaN payloads are
+// outside the bit-identity contract (quant.rs:2033-2044).
+__device__ __forceinline__ float h2f(uint32_t bits) {
+  return __half2float(__ushort_as_half((unsigned short)bits));
+}
+
+// One Q4_K superblock (raw GGUF layout, 144 B, 16-byte aligned in shared
+// memory) against the quantised activation block s of every batch row.
+// part[b] = d * xd * acc - dmin * xd * acc_m   (quant.rs:850-898)
+// High nibbles are dotted in place (q & 0xF0 = 16 * nibble) and the exact
+// sum is divided by 16 afterwards.
+template <int MAXB>
+__device__ __forceinline__ void q4k_superblock(const uint8_t* sb, int s, const KqParams& p,
+                                               const int8_t* xq, const float* xd, const int* bsum,
+                                               float* part) {
+  const uint4 hdr = lds_u4(sb);  // d | dmin, scales[0..12)
+  // get_scale_min_k4 (quant.rs:268-276) for all 8 sub-blocks.
+  int sc[8], mn[8];
 #pragma unroll
-  for (int k = 0; k < 8; k++) {
-    lo[k] = qw[k] & 0x0F0F0F0Fu;
-    hi[k] = (qw[k] >> 4) & 0x0F0F0F0Fu;
+  for (int j = 0; j < 4; j++) {
+    sc[j] = (hdr.y >> (8 * j)) & 63;
+    mn[j] = (hdr.z >> (8 * j)) & 63;
+    const uint32_t lo4 = (hdr.w >> (8 * j)) & 0xff;
+    sc[j + 4] = (lo4 & 15) | (((hdr.y >> (8 * j + 6)) & 3) << 4);
+    mn[j + 4] = (lo4 >> 4) | (((hdr.z >> (8 * j + 6)) & 3) << 4);
   }
-  const float d = f16_bits_to_f32(dw & 0xffffu), dmin = f16_bits_to_f32(dw >> 16);
-  for (int b = 0; b < p.batch; b++) {
-    const int8_t* xb = xq + (int64_t)b * p.n + s * 256 + 64 * h;
-    const int4 x0 = *reinterpret_cast<const int4*>(xb);
-    const int4 x1 = *reinterpret_cast<const int4*>(xb + 16);
-    const int4 x2 = *reinterpret_cast<const int4*>(xb + 32);
-    const int4 x3 = *reinterpret_cast<const int4*>(xb + 48);
-    int s_lo = 0, s_hi = 0;
-    s_lo = __dp4a((int)lo[0], x0.x, s_lo); s_lo = __dp4a((int)lo[1], x0.y, s_lo);
-    s_lo = __dp4a((int)lo[2], x0.z, s_lo); s_lo = __dp4a((int)lo[3], x0.w, s_lo);
-    s_lo = __dp4a((int)lo[4], x1.x, s_lo); s_lo = __dp4a((int)lo[5], x1.y, s_lo);
-    s_lo = __dp4a((int)lo[6], x1.z, s_lo); s_lo = __dp4a((int)lo[7], x1.w, s_lo);
-    s_hi = __dp4a((int)hi[0], x2.x, s_hi); s_hi = __dp4a((int)hi[1], x2.y, s_hi);
-    s_hi = __dp4a((int)hi[2], x2.z, s_hi); s_hi = __dp4a((int)hi[3], x2.w, s_hi);
-    s_hi = __dp4a((int)hi[4], x3.x, s_hi); s_hi = __dp4a((int)hi[5], x3.y, s_hi);
-    s_hi = __dp4a((int)hi[6], x3.z, s_hi); s_hi = __dp4a((int)hi[7], x3.w, s_hi);
-    const int blk = b * p.S + s;
-    int acc = sc0 * s_lo + sc1 * s_hi;
-    int accm = m0 * bsum[blk * 8 + 2 * h] + m1 * bsum[blk * 8 + 2 * h + 1];
-    acc += __shfl_xor_sync(FULL, acc, 1);
-    accm += __shfl_xor_sync(FULL, accm, 1);
-    acc += __shfl_xor_sync(FULL, acc, 2);
-    accm += __shfl_xor_sync(FULL, accm, 2);
-    if (valid && h == 0) {
-      // d * xq.d * acc as f32 - dmin * xq.d * acc_m as f32   (quant.rs:897)
+  int acc[MAXB];
+#pragma unroll
+  for (int b = 0; b < MAXB; b++) acc[b] = 0;
+#pragma unroll
+  for (int it = 0; it < 4; it++) {
+    const uint4 qa = lds_u4(sb + 16 + 32 * it), qb = lds_u4(sb + 32 + 32 * it);
+    const uint4 la = mask4(qa, 0x0F0F0F0Fu), lb = mask4(qb, 0x0F0F0F0Fu);
+    const uint4 ha = mask4(qa, 0xF0F0F0F0u), hb = mask4(qb, 0xF0F0F0F0u);
+#pragma unroll
+    for (int b = 0; b < MAXB; b++) {
+      if (b < p.batch) {
+        const int8_t* xb = xq + (b * p.S + s) * XQ_STRIDE + 64 * it;
+        const int s_lo = dot_ss(la, lds_i4(xb)) + dot_ss(lb, lds_i4(xb + 16));
+        const int s_hi16 = dot_us(ha, lds_i4(xb + 32)) + dot_us(hb, lds_i4(xb + 48));
+        acc[b] += sc[2 * it] * s_lo + sc[2 * it + 1] * (s_hi16 >> 4);
+      }
+    }
+  }
+  const float d = h2f(hdr.x & 0xffffu), dmin = h2f(hdr.x >> 16);
+#pragma unroll
+  for (int b = 0; b < MAXB; b++) {
+    if (b < p.batch) {
+      const int blk = b * p.S + s;
+      const int4 b0 = *reinterpret_cast<const int4*>(bsum + blk * 8);
+      const int4 b1 = *reinterpret_cast<const int4*>(bsum + blk * 8 + 4);
+      const int accm = mn[0] * b0.x + mn[1] * b0.y + mn[2] * b0.z + mn[3] * b0.w +
+                       mn[4] * b1.x + mn[5] * b1.y + mn[6] * b1.z + mn[7] * b1.w;
       const float xdv = xd[blk];
-      const float t0 = __fmul_rn(__fmul_rn(d, xdv), __int2float_rn(acc));
+      const float t0 = __fmul_rn(__fmul_rn(d, xdv), __int2float_rn(acc[b]));
       const float t1 = __fmul_rn(__fmul_rn(dmin, xdv), __int2float_rn(accm));
-      out[b * out_stride] = __fsub_rn(t0, t1);
+      part[b] = __fsub_rn(t0, t1);
     }
   }
 }
 
-__device__ __forceinline__ int sbyte(uint32_t w, int k) {  // sign-extended byte k
+// Sign-extended byte k of w.
+__device__ __forceinline__ int sbyte(uint32_t w, int k) {
   return ((int)(w << (24 - 8 * k))) >> 24;
 }
 
-// One Q6_K superblock (device SoA-8 group layout, see repack.cu). Lane
-// quarter j covers half h = j/2 and the 16-element runs l in [l0, l0+16),
-// l0 = 16 (j & 1): scale buckets 8h + (j&1) + {0, 2, 4, 6} (quant.rs:996-1057).
-// dp4a runs on the unsigned 6-bit codes; the -32 offset is applied exactly
-// through the per-16 activation sums: sum((q-32) x) = sum(q x) - 32 sum(x).
-__device__ __forceinline__ void q6k_unit(const uint8_t* row, int s, int j, const KqParams& p,
-                                         const int8_t* xq, const float* xd, const int* bsum,
-                                         float* out, int out_stride, bool valid) {
-  const int h = j >> 1, odd = j & 1, l0 = odd * 16;
-  const int gi = s >> 3, ii = s & 7;
-  const int G = min(8, p.S - gi * 8);
-  const uint8_t* gb = row + (int64_t)gi * 1680;
-  const uint4 A = *reinterpret_cast<const uint4*>(gb + 128 * ii + 64 * h + l0);
-  const uint4 B = *reinterpret_cast<const uint4*>(gb + 128 * ii + 64 * h + 32 + l0);
-  const uint4 H = *reinterpret_cast<const uint4*>(gb + 128 * G + 64 * ii + 32 * h + l0);
-  const uint2 SC = *reinterpret_cast<const uint2*>(gb + 192 * G + 16 * ii + 8 * h);
-  const uint32_t dbits = *reinterpret_cast<const uint16_t*>(gb + 208 * G + 2 * ii);
-  const int sc_t[4] = {sbyte(SC.x, odd), sbyte(SC.x, odd + 2), sbyte(SC.y, odd),
-                       sbyte(SC.y, odd + 2)};
-  const uint32_t a[4] = {A.x, A.y, A.z, A.w}, bb[4] = {B.x, B.y, B.z, B.w},
-                 hh[4] = {H.x, H.y, H.z, H.w};
-  uint32_t q[4][4];
+// One Q6_K superblock in the device layout (repack.cu): within a group of G
+// superblocks, ql chunk k (16 B) of superblock i is at 16 (G k + i), qh chunk k
+// at 128 G + 16 (G k + i), scales at 192 G + 16 i, d at 208 G + 2 i.
+// dp4a runs on the unsigned 6-bit codes; the -32 offset is applied exactly via
+// the per-16 activation sums: sum((q - 32) x) = sum(q x) - 32 sum(x).
+// part[b] = d * xd * acc   (quant.rs:996-1057)
+template <int MAXB>
+__device__ __forceinline__ void q6k_superblock(const uint8_t* gb, int G, int i, int s,
+                                               const KqParams& p, const int8_t* xq,
+                                               const float* xd, const int* bsum, float* part) {
+  const uint4 scw = lds_u4(gb + 192 * G + 16 * i);
+  const float d = h2f(*reinterpret_cast<const uint16_t*>(gb + 208 * G + 2 * i));
+  const uint32_t scv[4] = {scw.x, scw.y, scw.z, scw.w};
+  int sc[16];
 #pragma unroll
-  for (int k = 0; k < 4; k++) {
-    q[0][k] = (a[k] & 0x0F0F0F0Fu) | ((hh[k] & 0x03030303u) << 4);
-    q[1][k] = (bb[k] & 0x0F0F0F0Fu) | (((hh[k] >> 2) & 0x03030303u) << 4);
-    q[2][k] = ((a[k] >> 4) & 0x0F0F0F0Fu) | (((hh[k] >> 4) & 0x03030303u) << 4);
-    q[3][k] = ((bb[k] >> 4) & 0x0F0F0F0Fu) | (((hh[k] >> 6) & 0x03030303u) << 4);
-  }
-  const float d = f16_bits_to_f32(dbits);
-  for (int b = 0; b < p.batch; b++) {
-    const int blk = b * p.S + s;
-    const int8_t* xb = xq + (int64_t)b * p.n + s * 256 + 128 * h + l0;
-    int acc = 0;
+  for (int j = 0; j < 16; j++) sc[j] = sbyte(scv[j >> 2], j & 3);
+  int acc[MAXB];
 #pragma unroll
-    for (int t = 0; t < 4; t++) {
-      const int4 xv = *reinterpret_cast<const int4*>(xb + 32 * t);
-      int su = 0;
-      su = __dp4a((int)q[t][0], xv.x, su);
-      su = __dp4a((int)q[t][1], xv.y, su);
-      su = __dp4a((int)q[t][2], xv.z, su);
-      su = __dp4a((int)q[t][3], xv.w, su);
-      const int bucket = 8 * h + odd + 2 * t;
-      acc += sc_t[t] * (su - 32 * bsum[blk * 16 + bucket]);
+  for (int b = 0; b < MAXB; b++) acc[b] = 0;
+#pragma unroll
+  for (int h = 0; h < 2; h++) {
+#pragma unroll
+    for (int hc = 0; hc < 2; hc++) {  // l in [16 hc, 16 hc + 16)
+      const uint4 A = lds_u4(gb + 16 * (G * (4 * h + hc) + i));      // ql[64h + l]
+      const uint4 B = lds_u4(gb + 16 * (G * (4 * h + 2 + hc) + i));  // ql[64h + 32 + l]
+      const uint4 H = lds_u4(gb + 128 * G + 16 * (G * (2 * h + hc) + i));  // qh[32h + l]
+      const uint4 q1 = make_uint4((A.x & 0x0F0F0F0Fu) | ((H.x & 0x03030303u) << 4),
+                                  (A.y & 0x0F0F0F0Fu) | ((H.y & 0x03030303u) << 4),
+                                  (A.z & 0x0F0F0F0Fu) | ((H.z & 0x03030303u) << 4),
+                                  (A.w & 0x0F0F0F0Fu) | ((H.w & 0x03030303u) << 4));
+      const uint4 q2 = make_uint4((B.x & 0x0F0F0F0Fu) | ((H.x & 0x0C0C0C0Cu) << 2),
+                                  (B.y & 0x0F0F0F0Fu) | ((H.y & 0x0C0C0C0Cu) << 2),
+                                  (B.z & 0x0F0F0F0Fu) | ((H.z & 0x0C0C0C0Cu) << 2),
+                                  (B.w & 0x0F0F0F0Fu) | ((H.w & 0x0C0C0C0Cu) << 2));
+      const uint4 q3 = make_uint4(((A.x >> 4) & 0x0F0F0F0Fu) | (H.x & 0x30303030u),
+                                  ((A.y >> 4) & 0x0F0F0F0Fu) | (H.y & 0x30303030u),
+                                  ((A.z >> 4) & 0x0F0F0F0Fu) | (H.z & 0x30303030u),
+                                  ((A.w >> 4) & 0x0F0F0F0Fu) | (H.w & 0x30303030u));
+      const uint4 q4 = make_uint4(((B.x >> 4) & 0x0F0F0F0Fu) | ((H.x >> 2) & 0x30303030u),
+                                  ((B.y >> 4) & 0x0F0F0F0Fu) | ((H.y >> 2) & 0x30303030u),
+                                  ((B.z >> 4) & 0x0F0F0F0Fu) | ((H.z >> 2) & 0x30303030u),
+                                  ((B.w >> 4) & 0x0F0F0F0Fu) | ((H.w >> 2) & 0x30303030u));
+      const int j = 8 * h + hc;  // scale bucket of q1; q2 +2, q3 +4, q4 +6
+#pragma unroll
+      for (int b = 0; b < MAXB; b++) {
+        if (b < p.batch) {
+          const int8_t* xb = xq + (b * p.S + s) * XQ_STRIDE + 128 * h + 16 * hc;
+          acc[b] += sc[j] * dot_ss(q1, lds_i4(xb)) + sc[j + 2] * dot_ss(q2, lds_i4(xb + 32)) +
+                    sc[j + 4] * dot_ss(q3, lds_i4(xb + 64)) +
+                    sc[j + 6] * dot_ss(q4, lds_i4(xb + 96));
+        }
+      }
     }
-    acc += __shfl_xor_sync(FULL, acc, 1);
-    acc += __shfl_xor_sync(FULL, acc, 2);
-    if (valid && j == 0) {
-      // d * xq.d * acc as f32   (quant.rs:1056)
-      out[b * out_stride] = __fmul_rn(__fmul_rn(d, xd[blk]), __int2float_rn(acc));
+  }
+#pragma unroll
+  for (int b = 0; b < MAXB; b++) {
+    if (b < p.batch) {
+      const int blk = b * p.S + s;
+      int cor = 0;  // sum_j sc_j * (sum of the 16 activations of bucket j)
+#pragma unroll
+      for (int q = 0; q < 4; q++) {
+        const int4 bs = *reinterpret_cast<const int4*>(bsum + blk * 16 + 4 * q);
+        cor += sc[4 * q] * bs.x + sc[4 * q + 1] * bs.y + sc[4 * q + 2] * bs.z + sc[4 * q + 3] * bs.w;
+      }
+      const int total = acc[b] - 32 * cor;
+      part[b] = __fmul_rn(__fmul_rn(d, xd[blk]), __int2float_rn(total));
     }
   }
 }
 
-// fixed_tree (quant.rs:462-476) over part[0..len), len <= 128, by one warp.
-// Stride-doubling pairs index i with i + 2^k (i a multiple of 2^(k+1),
-// i + 2^k < len) -- the same additions as the reference's level-wise loop.
-__device__ __forceinline__ float warp_fixed_tree(const float* part, int stride, int len) {
-  const int lane = threadIdx.x & 31;
-  float v[4];
+// fixed_tree (quant.rs:462-476) over the `len` values of one row held by a
+// segment of `lpr` lanes (value i on segment lane i % 32, chunk i / 32).
+// Stride-doubling: index i (a multiple of 2^(k+1)) adds index i + 2^k when
+// that index is < len -- the same additions as the reference's level-wise loop.
+template <int NCH>
+__device__ __forceinline__ float seg_fixed_tree(float (&v)[NCH], int sl, int lpr, int len) {
+  for (int st = 1; st < lpr; st <<= 1) {
 #pragma unroll
-  for (int c = 0; c < 4; c++) {
-    const int i = c * 32 + lane;
-    v[c] = (i < len) ? part[i * stride] : 0.0f;
-  }
-#pragma unroll
-  for (int k = 0; k < 5; k++) {
-    const int st = 1 << k;
-#pragma unroll
-    for (int c = 0; c < 4; c++) {
+    for (int c = 0; c < NCH; c++) {
       const float o = __shfl_down_sync(FULL, v[c], st);
-      if ((lane & (2 * st - 1)) == 0 && c * 32 + lane + st < len) v[c] = __fadd_rn(v[c], o);
+      if ((sl & (2 * st - 1)) == 0 && c * 32 + sl + st < len) v[c] = __fadd_rn(v[c], o);
     }
   }
   float r = v[0];
-  if (lane == 0) {
+  if (NCH > 1) {
     if (32 < len) r = __fadd_rn(r, v[1]);
-    float r2 = v[2];
-    if (96 < len) r2 = __fadd_rn(r2, v[3]);
-    if (64 < len) r = __fadd_rn(r, r2);
+    if (NCH > 2) {
+      float r2 = v[2];
+      if (NCH > 3 && 96 < len) r2 = __fadd_rn(r2, v[3]);
+      if (64 < len) r = __fadd_rn(r, r2);
+    }
   }
-  return r;  // valid in lane 0
+  return r;  // valid on segment lane 0
 }
 
-template <int QT>  // 0 = Q4_K, 1 = Q6_K
-__global__ void __launch_bounds__(KQ_THREADS, 1) kq_matvec_kernel(const KqParams p) {
+// One warp pass: rows rr0 + seg of the stage buffer.
+template <int QT, int MAXB, int NCH>
+__device__ __forceinline__ void consume_pass(const KqParams& p, const uint8_t* sbuf, int rr,
+                                             bool row_ok, int sl, int64_t yrow,
+                                             const int8_t* xq, const float* xd, const int* bsum) {
+  float part[NCH][MAXB];
+#pragma unroll
+  for (int c = 0; c < NCH; c++) {
+    const int s = c * 32 + sl;
+#pragma unroll
+    for (int b = 0; b < MAXB; b++) part[c][b] = 0.0f;
+    if (row_ok && s < p.S) {
+      const uint8_t* row = sbuf + (int64_t)rr * p.pitch;
+      if (QT == 0) {
+        q4k_superblock<MAXB>(row + s * 144, s, p, xq, xd, bsum, part[c]);
+      } else {
+        const int gi = s >> 3;
+        q6k_superblock<MAXB>(row + gi * 1680, min(8, p.S - 8 * gi), s & 7, s, p, xq, xd, bsum,
+                             part[c]);
+      }
+    }
+  }
+#pragma unroll
+  for (int b = 0; b < MAXB; b++) {
+    if (b < p.batch) {
+      float v[NCH];
+#pragma unroll
+      for (int c = 0; c < NCH; c++) v[c] = part[c][b];
+      const float t = seg_fixed_tree<NCH>(v, sl, p.lpr, p.S);
+      if (row_ok && sl == 0) p.y[(int64_t)b * p.ldy + yrow] = t;
+    }
+  }
+}
+
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_launch() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+template <int QT, int MAXB, int NCH, int CW>
+__global__ void __launch_bounds__((CW + 1) * 32, 1) kq_matvec_kernel(const KqParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+  uint64_t* empty = full + KQ_NST_MAX;
+  uint64_t* xbar = empty + KQ_NST_MAX;
   float* xd = reinterpret_cast<float*>(smem + p.off_xd);
   int* bsum = reinterpret_cast<int*>(smem + p.off_bsum);
-  float* part = reinterpret_cast<float*>(smem + p.off_part);
   int8_t* xq = reinterpret_cast<int8_t*>(smem + p.off_xq);
+  float* xf = reinterpret_cast<float*>(smem + p.off_xf);
   uint8_t* stg = smem + p.off_stage;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int r0 = (int)((int64_t)blockIdx.x * p.R / gridDim.x);
-  const int r1 = (int)((int64_t)(blockIdx.x + 1) * p.R / gridDim.x);
-  const int nstages = (r1 - r0 + p.rps - 1) / p.rps;
+  const int bid = blockIdx.x;
+  const int r0 = bid * p.rows_base + min(bid, p.rows_rem);
+  const int nrows = p.rows_base + (bid < p.rows_rem ? 1 : 0);
+  const int nstages = (nrows + p.rps - 1) / p.rps;
 
   if (tid == 0) {
-    for (int i = 0; i < p.nst; i++) mbar_init(&full[i], 1);
+    KQ_TRACE(0);
+    KQ_TRACE(6);
+    for (int i = 0; i < p.nst; i++) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], CW);
+    }
+    mbar_init(xbar, 1);
     fence_mbar_init();
   }
   __syncthreads();
-  const uint64_t pol = policy_evict_first();
-  auto issue = [&](int k) {
-    const int ra = r0 + k * p.rps, rb = min(ra + p.rps, r1);
-    const uint32_t bytes = (uint32_t)((rb - ra) * p.pitch);
-    const int buf = k % p.nst;
-    mbar_arrive_expect_tx(&full[buf], bytes);
-    bulk_g2s_stream(stg + (size_t)buf * p.stage_bytes, p.W + (int64_t)ra * p.pitch, bytes,
-                    &full[buf], pol);
-  };
-  if (tid == 0)
-    for (int k = 0; k < min(p.nst, nstages); k++) issue(k);
 
-  quantize_x<QT == 0 ? 8 : 16>(p, xd, bsum, xq);
-  __syncthreads();
-
-  const int part_sz = p.rps * p.S * p.batch;
-  for (int k = 0; k < nstages; k++) {
-    const int buf = k % p.nst;
-    const bool ok = mbar_wait_bounded(&full[buf], (uint32_t)((k / p.nst) & 1));
-    const int ra = r0 + k * p.rps, rows = min(p.rps, r1 - ra);
-    float* pb = part + (k & 1) * part_sz;
-    const uint8_t* sbuf = stg + (size_t)buf * p.stage_bytes;
-    if (ok) {
-      const int U = rows * p.S;
-      for (int u0 = warp * 8; u0 < U; u0 += KQ_WARPS * 8) {
-        int u = u0 + (lane >> 2);
-        const bool valid = u < U;
-        if (!valid) u = U - 1;
-        const int rr = u / p.S, s = u - rr * p.S;
-        float* out = pb + (rr * p.S + s) * p.batch;
-        if (QT == 0)
-          q4k_unit(sbuf + (int64_t)rr * p.pitch + s * 144, lane & 3, p, xq, xd, bsum, s, out, 1,
-                   valid);
-        else
-          q6k_unit(sbuf + (int64_t)rr * p.pitch, s, lane & 3, p, xq, xd, bsum, out, 1, valid);
+  if (warp == CW) {
+    // ---- producer: one thread streams x, then the CTA's rows, through TMA ----
+    if (lane == 0) {
+      const uint64_t pol = policy_evict_first();
+      auto issue = [&](int k) {
+        const int buf = k % p.nst;
+        const int ra = k * p.rps, rb = min(ra + p.rps, nrows);
+        const uint32_t bytes = (uint32_t)((rb - ra) * p.pitch);
+        mbar_arrive_expect_tx(&full[buf], bytes);
+        bulk_g2s_stream(stg + (size_t)buf * p.stage_bytes, p.W + (int64_t)(r0 + ra) * p.pitch,
+                        bytes, &full[buf], pol);
+      };
+      // Weights are never written by a preceding kernel: stream the first
+      // stages before waiting on the previous grid (programmatic launch).
+      const int first = min(p.nst, nstages);
+      if (first > 0) issue(0);
+      grid_dep_wait();
+      if (p.x_smem) {
+        const uint32_t rowb = (uint32_t)p.n * 4u;
+        mbar_arrive_expect_tx(xbar, rowb * p.batch);
+        for (int b = 0; b < p.batch; b++) bulk_g2s(xf + (size_t)b * p.n, p.x + b * p.ldx, rowb, xbar);
+      }
+      for (int k = 1; k < first; k++) issue(k);
+      KQ_TRACE(1);
+      grid_dep_launch();
+      for (int k = first; k < nstages; k++) {
+        const int buf = k % p.nst;
+        if (!mbar_wait_bounded(&empty[buf], (uint32_t)(((k / p.nst) - 1) & 1))) {
+          record_error(p.status, KERR_TIMEOUT);
+          for (int j = max(0, k - p.nst); j < k; j++)  // drain copies already issued
+            mbar_wait_bounded(&full[j % p.nst], (uint32_t)((j / p.nst) & 1));
+          if (p.x_smem) mbar_wait_bounded(xbar, 0);
+          return;
+        }
+        issue(k);
       }
     }
-    if (__syncthreads_or(!ok)) {
-      if (tid == 0) {
-        record_error(p.status, KERR_TIMEOUT);
-        for (int j = k; j < min(k + p.nst, nstages); j++)
-          mbar_wait_bounded(&full[j % p.nst], (uint32_t)((j / p.nst) & 1));
-      }
+    return;
+  }
+
+  // ---- consumers ----
+  const float* xs = p.x;
+  int64_t xstride = p.ldx;
+  if (p.x_smem) {
+    if (!mbar_wait_bounded(xbar, 0)) {
+      if (lane == 0) record_error(p.status, KERR_TIMEOUT);
       return;
     }
-    if (tid == 0 && k + p.nst < nstages) issue(k + p.nst);
-    for (int t = warp; t < rows * p.batch; t += KQ_WARPS) {
-      const int rr = t / p.batch, b = t - rr * p.batch;
-      const float v = warp_fixed_tree(pb + rr * p.S * p.batch + b, p.batch, p.S);
-      if (lane == 0) p.y[(int64_t)b * p.ldy + ra + rr] = v;
+    xs = xf;
+    xstride = p.n;
+    if (tid == 0) KQ_TRACE(4);
+  } else {
+    grid_dep_wait();
+  }
+  quantize_x<QT == 0 ? 8 : 16, CW>(p, xs, xstride, warp, lane, xd, bsum, xq);
+  asm volatile("bar.sync 1, %0;" ::"n"(CW * 32));
+  if (tid == 0) KQ_TRACE(2);
+
+  // Row groups of rpw rows (one warp pass) are dealt to warps round-robin
+  // across the whole CTA range, so warps work on different stages at once.
+  const int rpw = 32 / p.lpr;
+  const int seg = lane / p.lpr, sl = lane - seg * p.lpr;
+  const int gps = p.rps / rpw;  // groups per stage
+  int g = warp;                 // next group of this warp
+  for (int k = 0; k < nstages; k++) {
+    const int buf = k % p.nst;
+    const int gend = min((k + 1) * gps, (nrows + rpw - 1) / rpw);
+    if (g < gend) {
+      if (!mbar_wait_bounded(&full[buf], (uint32_t)((k / p.nst) & 1))) {
+        if (lane == 0) record_error(p.status, KERR_TIMEOUT);
+        return;
+      }
+      if (tid == 0 && k == 0) KQ_TRACE(3);
+      const uint8_t* sbuf = stg + (size_t)buf * p.stage_bytes;
+      for (; g < gend; g += CW) {
+        const int r = g * rpw + seg;  // CTA-local row
+        consume_pass<QT, MAXB, NCH>(p, sbuf, r - k * p.rps, r < nrows, sl, r0 + r, xq, xd, bsum);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) {
+      asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&empty[buf]))
+                   : "memory");
     }
   }
+  if (tid == 0) KQ_TRACE(5);
+}
+
+bool use_pdl() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("VTQ_NO_PDL");
+    v = (e && *e && *e != '0') ? 0 : 1;
+  }
+  return v == 1;
+}
+
+template <int QT, int MAXB, int NCH, int CW>
+cudaError_t launch_variant(const KqParams& p, int grid, uint32_t smem, cudaStream_t st) {
+  static bool attr_set = false;  // opt-in shared memory, once per instantiation
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(kq_matvec_kernel<QT, MAXB, NCH, CW>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         max_smem_optin());
+    if (e != cudaSuccess) return e;
+    attr_set = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3((CW + 1) * 32);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = use_pdl() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kq_matvec_kernel<QT, MAXB, NCH, CW>, p);
+}
+
+template <int QT, int MAXB>
+cudaError_t launch_nch(const KqParams& p, int grid, uint32_t smem, cudaStream_t st) {
+  const int nch = (p.S + 31) / 32;
+  constexpr int CW = MAXB <= 2 ? 16 : 8;
+  if (nch <= 1) return launch_variant<QT, MAXB, 1, CW>(p, grid, smem, st);
+  if (nch == 2) return launch_variant<QT, MAXB, 2, CW>(p, grid, smem, st);
+  return launch_variant<QT, MAXB, 4, CW>(p, grid, smem, st);
+}
+
+template <int QT>
+cudaError_t launch_qt(const KqParams& p, int grid, uint32_t smem, cudaStream_t st) {
+  if (p.batch <= 1) return launch_nch<QT, 1>(p, grid, smem, st);
+  if (p.batch <= 2) return launch_nch<QT, 2>(p, grid, smem, st);
+  return launch_nch<QT, 4>(p, grid, smem, st);
 }
 
 }  // namespace
@@ -364,12 +545,17 @@ static inline uint32_t align_up(uint32_t v, uint32_t a) { return (v + a - 1) / a
 
 cudaError_t launch_kq_matvec(const DevMatrix& m, const float* x, int64_t ldx, int64_t batch,
                              float* y, int64_t ldy, unsigned* status, cudaStream_t st) {
+  constexpr int KQ_BMAX = 4;  // activation rows per launch
   if (m.dtype != T_Q4_K && m.dtype != T_Q6_K) return cudaErrorInvalidValue;
   const int S = (int)(m.in_feat / 256);
   if (S < 1 || S > KQ_SMAX || m.in_feat % 256) return cudaErrorInvalidValue;
   if (m.out_feat <= 0 || batch <= 0) return cudaSuccess;
   const int smem_max = max_smem_optin();
   const int nsm = num_sms();
+  int lpr = 1;
+  while (lpr < S && lpr < 32) lpr <<= 1;
+  const int rpw = 32 / lpr;
+  const int grid = (int)std::min<int64_t>(m.out_feat, nsm);
   for (int64_t b0 = 0; b0 < batch; b0 += KQ_BMAX) {
     const int nb = (int)std::min<int64_t>(KQ_BMAX, batch - b0);
     KqParams p{};
@@ -381,55 +567,50 @@ cudaError_t launch_kq_matvec(const DevMatrix& m, const float* x, int64_t ldx, in
     p.W = m.data;
     p.pitch = m.pitch;
     p.R = (int)m.out_feat;
+    p.rows_base = p.R / grid;
+    p.rows_rem = p.R % grid;
     p.y = y + b0 * ldy;
     p.ldy = ldy;
     p.status = status;
+    p.lpr = lpr;
     const int NB = m.dtype == T_Q4_K ? 8 : 16;
-    uint32_t off = align_up(KQ_NST_MAX * 8, 16);
+    uint32_t off = 256;  // mbarriers
     p.off_xd = off;
     off = align_up(off + nb * S * 4, 16);
     p.off_bsum = off;
     off = align_up(off + nb * S * NB * 4, 16);
     p.off_xq = off;
-    off = align_up(off + nb * p.n, 128);
-    // Stage = whole rows, about 24 KB; part double buffer sized to match.
-    int rps = std::max<int>(1, (int)(24576 / m.pitch));
-    const int rows_per_cta = (int)((m.out_feat + nsm - 1) / nsm);
-    rps = std::min(rps, rows_per_cta);
+    off = align_up(off + nb * S * XQ_STRIDE, 128);
+    // Stage x through TMA when every row start is 16-byte aligned and it fits.
+    const uint32_t xbytes = (uint32_t)(nb * p.n * 4);
+    p.x_smem = ((reinterpret_cast<uintptr_t>(p.x) & 15u) == 0 && (ldx % 4) == 0 &&
+                xbytes <= 65536u) ? 1 : 0;
+    p.off_xf = off;
+    if (p.x_smem) off = align_up(off + xbytes, 128);
+    p.off_stage = off;
+    // Stages of ~24 KB of whole warp passes (TMA streams at full rate from 16 KB).
+    const int rows_per_cta = p.rows_base + (p.rows_rem ? 1 : 0);
+    int rps = std::max(rpw, (int)(24576 / m.pitch) / rpw * rpw);
+    rps = std::min(rps, (rows_per_cta + rpw - 1) / rpw * rpw);
     int nst;
     for (;;) {
-      const uint32_t part_bytes = align_up(2u * rps * S * nb * 4, 128);
       const uint32_t stage_bytes = (uint32_t)(rps * m.pitch);
-      const int avail = smem_max - (int)off - (int)part_bytes;
+      const int avail = smem_max - (int)off;
       nst = std::min<int>(KQ_NST_MAX, avail > 0 ? avail / (int)stage_bytes : 0);
       const int need = (rows_per_cta + rps - 1) / rps;  // stages per CTA
       nst = std::min(nst, std::max(need, 1));
       if (nst >= 2 || (nst >= 1 && need <= 1)) {
-        p.off_part = off;
-        p.off_stage = off + part_bytes;
         p.stage_bytes = stage_bytes;
         break;
       }
-      if (rps == 1) return cudaErrorInvalidValue;  // row too long for shared memory
-      rps = std::max(1, rps / 2);
+      if (rps <= rpw) return cudaErrorInvalidValue;  // rows too long for shared memory
+      rps = std::max(rpw, rps / 2 / rpw * rpw);
     }
     p.rps = rps;
     p.nst = nst;
     const uint32_t smem = p.off_stage + (uint32_t)nst * p.stage_bytes;
-    const int grid = (int)std::min<int64_t>(m.out_feat, nsm);
-    cudaError_t e;
-    // The opt-in size is set once per kernel (per process) to the device maximum.
-    static bool attr_set[2] = {false, false};
-    const int qi = m.dtype == T_Q4_K ? 0 : 1;
-    if (!attr_set[qi]) {
-      e = cudaFuncSetAttribute(qi == 0 ? kq_matvec_kernel<0> : kq_matvec_kernel<1>,
-                               cudaFuncAttributeMaxDynamicSharedMemorySize, smem_max);
-      if (e != cudaSuccess) return e;
-      attr_set[qi] = true;
-    }
-    if (qi == 0) kq_matvec_kernel<0><<<grid, KQ_THREADS, smem, st>>>(p);
-    else kq_matvec_kernel<1><<<grid, KQ_THREADS, smem, st>>>(p);
-    e = cudaGetLastError();
+    const cudaError_t e = m.dtype == T_Q4_K ? launch_qt<0>(p, grid, smem, st)
+                                            : launch_qt<1>(p, grid, smem, st);
     if (e != cudaSuccess) return e;
   }
   return cudaSuccess;

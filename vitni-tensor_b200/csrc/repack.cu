@@ -4,10 +4,13 @@
 // zero padding after the packed row bytes.
 // Q6_K additionally: within a row, superblocks are grouped in runs of 8
 // (the last run may be shorter, G = min(8, S - 8g)) and each run is stored
-// field by field -- ql[G][128], qh[G][64], scales[G][16], d[G][2] -- so that
-// every field of every superblock starts on a 16-byte boundary (210 * 8 = 1680
-// = 105 * 16). The bytes are a permutation of the GGUF bytes: nothing is
-// converted, so the integer kernel reads exactly the reference's values.
+// field by field: ql as 8 chunks of 16 bytes per superblock with chunk k of
+// superblock i at slot G k + i, then qh the same way (4 chunks each), then
+// the 16 scale bytes of each superblock, then the 2-byte d values. Every
+// field starts on a 16-byte boundary (210 * 8 = 1680 = 105 * 16), and lanes
+// that read chunk k of consecutive superblocks touch consecutive 16-byte
+// slots (no shared-memory bank conflicts). The bytes are a permutation of the
+// GGUF bytes: nothing is converted, so the kernel reads the reference's values.
 #include "vtq_device.cuh"
 #include "vtq_internal.h"
 
@@ -46,10 +49,21 @@ __global__ void repack_kernel(const uint8_t* __restrict__ src, uint8_t* __restri
         const int gi = (int)(o / 1680), w = (int)(o - (int64_t)gi * 1680);
         const int G = min(8, S - 8 * gi);
         int ii, f;
-        if (w < 128 * G) { ii = w / 128; f = w % 128; }
-        else if (w < 192 * G) { ii = (w - 128 * G) / 64; f = 128 + (w - 128 * G) % 64; }
-        else if (w < 208 * G) { ii = (w - 192 * G) / 16; f = 192 + (w - 192 * G) % 16; }
-        else { ii = (w - 208 * G) / 2; f = 208 + (w - 208 * G) % 2; }
+        if (w < 128 * G) {  // ql: 16-byte chunk k of superblock i at slot G k + i
+          const int slot = w / 16;
+          ii = slot % G;
+          f = 16 * (slot / G) + w % 16;
+        } else if (w < 192 * G) {  // qh: same interleave, 4 chunks per superblock
+          const int v = w - 128 * G, slot = v / 16;
+          ii = slot % G;
+          f = 128 + 16 * (slot / G) + v % 16;
+        } else if (w < 208 * G) {  // scales: 16 bytes per superblock
+          ii = (w - 192 * G) / 16;
+          f = 192 + (w - 192 * G) % 16;
+        } else {  // d: 2 bytes per superblock
+          ii = (w - 208 * G) / 2;
+          f = 208 + (w - 208 * G) % 2;
+        }
         so = (int64_t)(8 * gi + ii) * 210 + f;
       }
       v = src[r * row_bytes + so];

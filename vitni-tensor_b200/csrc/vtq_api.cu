@@ -25,7 +25,7 @@ struct vtq_ctx {
 };
 
 struct vtq_weight {
-  vtq_ctx* ctx = nullptr;
+  int device = 0;  // the owning context may be destroyed before the weight
   DevMatrix m{};
   uint8_t* buf = nullptr;
   size_t bytes = 0;
@@ -131,7 +131,7 @@ vtq_status linear_host(vtq_ctx* c, const DevMatrix& m, const float* x, float* y,
 vtq_status upload(vtq_ctx* c, int dtype, const uint8_t* bytes, int64_t in_feat, int64_t row0,
                   int64_t rows, vtq_weight** out) {
   auto* w = new vtq_weight();
-  w->ctx = c;
+  w->device = c->device;
   w->m.dtype = dtype;
   w->m.in_feat = in_feat;
   w->m.out_feat = rows;
@@ -266,9 +266,8 @@ vtq_status vtq_weight_upload(vtq_ctx* c, int32_t dtype, const uint8_t* bytes, si
 
 vtq_status vtq_weight_free(vtq_weight* w) {
   if (!w) return VTQ_ERR_INVALID_ARG;
-  cudaSetDevice(w->ctx->device);
-  cudaStreamSynchronize(w->ctx->stream);
-  cudaFree(w->buf);
+  cudaSetDevice(w->device);
+  cudaFree(w->buf);  // cudaFree waits for work in flight on the device
   delete w;
   return VTQ_OK;
 }
