@@ -210,6 +210,9 @@ def main():
     ap.add_argument("--config", default="c2_q4_k_llama7b_ffn")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--check", action="store_true", help="bit-compare outputs with the oracle")
+    ap.add_argument("--launches-only", action="store_true",
+                    help="profiling mode: one weight copy, W + K plain launches per matvec, "
+                         "no graph, no timing output (for ncu captures)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     world, rank, local = setup_dist()
@@ -235,6 +238,8 @@ def main():
     step_bytes = sum(algo_bytes(dt, n, r) for dt, n, r in cfg)
     wbytes = sum(r * vtq.row_bytes(dt, n) for dt, n, r in cfg)
     copies = max(1, -(-ROTATE_MIN_BYTES // wbytes))
+    if args.launches_only:
+        copies = 1
     host_w = [synth.weight(dt, f"{args.config}.w.{n}x{r}", r, n) for dt, n, r in cfg]
     host_x = [synth.activation(f"{args.config}.x.{n}", 1, n) for dt, n, r in cfg]
     weights = [[ctx.upload(dt, host_w[i], n, r) for i, (dt, n, r) in enumerate(cfg)]
@@ -255,6 +260,13 @@ def main():
 
     rotation()
     torch.cuda.synchronize()
+    if args.launches_only:
+        for _ in range(args.warmup + args.steps - 1):
+            rotation()
+        torch.cuda.synchronize()
+        print(json.dumps({"launches_only": True, "config": args.config,
+                          "launches": (args.warmup + args.steps) * len(cfg)}))
+        return
     if args.check:
         from oracle import oracle as O
         for i, (dt, n, r) in enumerate(cfg):

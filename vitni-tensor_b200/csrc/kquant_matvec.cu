@@ -38,6 +38,9 @@ namespace {
 constexpr int KQ_NST_MAX = 16;                   // ring depth
 constexpr int KQ_SMAX = 128;                     // superblocks per row (in_feat <= 32768)
 constexpr int XQ_STRIDE = 272;                   // padded bytes per quantised activation block
+// Activation-sum records per block, padded by 4 ints so that 8 lanes reading
+// 8 consecutive blocks' records hit 8 different groups of 4 banks.
+template <int NB> struct BsumStride { static constexpr int v = NB + 4; };
 constexpr uint32_t FULL = 0xffffffffu;
 
 #ifdef VTQ_TRACE
@@ -110,9 +113,9 @@ __device__ __forceinline__ void quantize_x(const KqParams& p, const float* xs, i
     const int s32 = s16 + __shfl_xor_sync(FULL, s16, 2);
     const int blk = b * p.S + s;
     if (NB == 8) {
-      if ((lane & 3) == 0) bsum[blk * 8 + (lane >> 2)] = s32;
+      if ((lane & 3) == 0) bsum[blk * BsumStride<8>::v + (lane >> 2)] = s32;
     } else {
-      if ((lane & 1) == 0) bsum[blk * 16 + (lane >> 1)] = s16;
+      if ((lane & 1) == 0) bsum[blk * BsumStride<16>::v + (lane >> 1)] = s16;
     }
     *reinterpret_cast<uint2*>(xq + blk * XQ_STRIDE + lane * 8) = make_uint2(w0, w1);
     if (lane == 0) xd[blk] = d;
@@ -202,8 +205,8 @@ __device__ __forceinline__ void q4k_superblock(const uint8_t* sb, int s, const K
   for (int b = 0; b < MAXB; b++) {
     if (b < p.batch) {
       const int blk = b * p.S + s;
-      const int4 b0 = *reinterpret_cast<const int4*>(bsum + blk * 8);
-      const int4 b1 = *reinterpret_cast<const int4*>(bsum + blk * 8 + 4);
+      const int4 b0 = *reinterpret_cast<const int4*>(bsum + blk * BsumStride<8>::v);
+      const int4 b1 = *reinterpret_cast<const int4*>(bsum + blk * BsumStride<8>::v + 4);
       const int accm = mn[0] * b0.x + mn[1] * b0.y + mn[2] * b0.z + mn[3] * b0.w +
                        mn[4] * b1.x + mn[5] * b1.y + mn[6] * b1.z + mn[7] * b1.w;
       const float xdv = xd[blk];
@@ -280,7 +283,7 @@ __device__ __forceinline__ void q6k_superblock(const uint8_t* gb, int G, int i, 
       int cor = 0;  // sum_j sc_j * (sum of the 16 activations of bucket j)
 #pragma unroll
       for (int q = 0; q < 4; q++) {
-        const int4 bs = *reinterpret_cast<const int4*>(bsum + blk * 16 + 4 * q);
+        const int4 bs = *reinterpret_cast<const int4*>(bsum + blk * BsumStride<16>::v + 4 * q);
         cor += sc[4 * q] * bs.x + sc[4 * q + 1] * bs.y + sc[4 * q + 2] * bs.z + sc[4 * q + 3] * bs.w;
       }
       const int total = acc[b] - 32 * cor;
@@ -573,7 +576,7 @@ cudaError_t launch_kq_matvec(const DevMatrix& m, const float* x, int64_t ldx, in
     p.ldy = ldy;
     p.status = status;
     p.lpr = lpr;
-    const int NB = m.dtype == T_Q4_K ? 8 : 16;
+    const int NB = m.dtype == T_Q4_K ? BsumStride<8>::v : BsumStride<16>::v;
     uint32_t off = 256;  // mbarriers
     p.off_xd = off;
     off = align_up(off + nb * S * 4, 16);
