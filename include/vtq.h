@@ -128,6 +128,38 @@ vtq_status vtq_linear_device(int32_t dtype, const uint8_t* w_dev, int64_t in_fea
                              int64_t batch, uint32_t flags, uint32_t* status_dev,
                              void* cuda_stream);
 
+/* ---- Quantized decode session: a GGUF Llama model resident on
+ * one device; the decode step of src/model/forward_quantized.rs:329-649 and the
+ * prompt + greedy loop of src/model/inference.rs:312-327 run as one CUDA graph
+ * per step with the position and current token in device memory. ---- */
+typedef struct vtq_decode vtq_decode;
+/* Parse the GGUF blob (src/model/gguf.rs:305-422, config.rs:156-212,
+ * quant_weights.rs:121-181) and upload every tensor. On failure *out still
+ * receives a handle carrying the message (vtq_decode_last_error); close it. */
+vtq_status vtq_decode_open(vtq_ctx* ctx, int device, const uint8_t* gguf, size_t len,
+                           vtq_decode** out);
+const char* vtq_decode_last_error(const vtq_decode* d);
+/* dim, hidden, layers, heads, kv_heads, vocab, seq_len, shared_weights. */
+vtq_status vtq_decode_config(const vtq_decode* d, int64_t* out8);
+/* run_quantized's token loop (inference.rs:312-327): out_tokens receives the
+ * n_new generated ids; logits (optional) receives (n_prompt + n_new) x vocab. */
+vtq_status vtq_decode_run(vtq_decode* d, const uint32_t* prompt, size_t n_prompt, size_t n_new,
+                          uint32_t* out_tokens, float* logits);
+vtq_status vtq_decode_close(vtq_decode* d);
+
+/* ---- Software transcendentals shared by host and device. ----
+ * Bit-for-bit the single-precision functions of the Rust `libm` crate the
+ * reference calls (Cargo.toml:23): expf (forward_quantized.rs:559, :934),
+ * sinf / cosf / powf (RoPE, forward_quantized.rs:453-456). */
+float vtq_expf(float x);
+float vtq_sinf(float x);
+float vtq_cosf(float x);
+float vtq_powf(float x, float y);
+/* For each in[i], the 7 values the reference's determinism sweep hashes
+ * (tests/transcendental_determinism.rs:36-44): expf, sqrtf(|v|), cosf, sinf,
+ * powf(1e4, v/64), powf(1e6, v/64), 1/(1+expf(-v)); out holds 7*n floats. */
+void vtq_libm_sweep(const float* in, size_t n, float* out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -198,3 +198,76 @@ def argmax(x) -> int:
 
 def matmul_fnv_golden() -> int:
     return int(lib().or_matmul_fnv_golden())
+
+
+# ---- decode step / run loop (vtq_oracle_decode.cpp) -------------------------
+
+class _Tensor(ctypes.Structure):
+    _fields_ = [("dtype", ctypes.c_int32), ("bytes", ctypes.c_void_p), ("len", ctypes.c_size_t)]
+
+
+class _Layer(ctypes.Structure):
+    _fields_ = [("rms_att", ctypes.c_void_p), ("rms_ffn", ctypes.c_void_p)] + \
+        [(n, _Tensor) for n in ("wq", "wk", "wv", "wo", "w1", "w2", "w3")]
+
+
+class _Model(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int32) for n in ("dim", "hidden", "n_layers", "n_heads",
+                                               "n_kv_heads", "vocab", "seq_len")] + \
+        [("rope_theta", ctypes.c_float), ("rms_eps", ctypes.c_float), ("embd", _Tensor),
+         ("rms_final", ctypes.c_void_p), ("wcls", _Tensor), ("layers", ctypes.c_void_p)]
+
+
+def decode_run(gguf_blob: bytes, prompt, n_new: int, threads: int = 8, logits: bool = False):
+    """The reference's run_quantized token loop on the CPU (oracle)."""
+    import sys as _sys
+    pkg = os.path.join(os.path.dirname(HERE), "vitni-tensor_b200")
+    if pkg not in _sys.path:
+        _sys.path.insert(0, pkg)
+    from vtq import gguf as G
+    g = G.read(gguf_blob)
+    meta, ts = g["metadata"], g["tensors"]
+    keep = []
+
+    def addr(name):
+        arr = np.frombuffer(ts[name][2], np.uint8)
+        keep.append(arr)
+        return arr.ctypes.data, arr.nbytes
+
+    def tensor(name):
+        p, n = addr(name)
+        return _Tensor(ts[name][1], p, n)
+
+    arch = meta["general.architecture"]
+    m = _Model()
+    m.dim = meta[f"{arch}.embedding_length"]
+    m.hidden = meta[f"{arch}.feed_forward_length"]
+    m.n_layers = meta[f"{arch}.block_count"]
+    m.n_heads = meta[f"{arch}.attention.head_count"]
+    m.n_kv_heads = meta.get(f"{arch}.attention.head_count_kv", m.n_heads)
+    m.vocab = meta[f"{arch}.vocab_size"]
+    m.seq_len = meta[f"{arch}.context_length"]
+    m.rope_theta = meta.get(f"{arch}.rope.freq_base", 10000.0)
+    m.rms_eps = meta.get(f"{arch}.attention.layer_norm_rms_epsilon", 1e-5)
+    m.embd = tensor("token_embd.weight")
+    m.rms_final = addr("output_norm.weight")[0]
+    m.wcls = tensor("output.weight") if "output.weight" in ts else _Tensor(0, None, 0)
+    layers = (_Layer * m.n_layers)()
+    for l in range(m.n_layers):
+        p = f"blk.{l}."
+        layers[l].rms_att = addr(p + "attn_norm.weight")[0]
+        layers[l].rms_ffn = addr(p + "ffn_norm.weight")[0]
+        for fld, nm in (("wq", "attn_q"), ("wk", "attn_k"), ("wv", "attn_v"),
+                        ("wo", "attn_output"), ("w1", "ffn_gate"), ("w2", "ffn_down"),
+                        ("w3", "ffn_up")):
+            setattr(layers[l], fld, tensor(p + nm + ".weight"))
+    m.layers = ctypes.cast(layers, ctypes.c_void_p)
+    pr = np.ascontiguousarray(prompt, dtype=np.uint32)
+    out = np.zeros(max(1, n_new), np.uint32)
+    lg = np.zeros((len(pr) + n_new, m.vocab), np.float32) if logits else None
+    fn = lib().or_decode_run
+    fn.argtypes = [ctypes.POINTER(_Model), ctypes.c_void_p, ctypes.c_size_t, ctypes.c_size_t,
+                   ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int]
+    _chk(fn(ctypes.byref(m), pr.ctypes.data, len(pr), n_new, out.ctypes.data,
+            lg.ctypes.data if lg is not None else None, threads))
+    return out[:n_new].tolist(), lg

@@ -1,0 +1,72 @@
+"""Device decode session vs the CPU oracle of the reference's decode step:
+per-step logits bit-exact, generated tokens and receipt digests identical
+(BASELINE config 4 and smaller models through the same code)."""
+import numpy as np
+import pytest
+
+import vtq
+from vtq import gguf, receipt
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+SMALL = dict(dim=256, hidden=512, layers=2, heads=4, kv_heads=2, vocab=300, seq_len=64,
+             rope_theta=10000.0, rms_eps=1e-5)
+
+
+def run_both(blob, prompt, n_new):
+    sess = vtq.DecodeSession(blob)
+    got, lg = sess.run(prompt, n_new, logits=True)
+    again, _ = sess.run(prompt, n_new)  # a second run (graph without the logits log)
+    sess.close()
+    ref, rlg = O.decode_run(blob, prompt, n_new, threads=8, logits=True)
+    return got, lg, again, ref, rlg
+
+
+def assert_bits(a, b):
+    bad = np.nonzero(a.reshape(-1).view(np.uint32) != b.reshape(-1).view(np.uint32))[0]
+    assert bad.size == 0, f"{bad.size} logits differ; first {bad[:4]}"
+
+
+@pytest.mark.parametrize("variant", ["q4k_embd", "q6k_embd", "shared_head", "mha"])
+def test_small_models_bit_exact(variant):
+    cfg = dict(SMALL)
+    kw = {}
+    if variant == "q6k_embd":
+        kw["embd_dtype"] = vtq.Q6_K
+    if variant == "shared_head":
+        kw["shared_head"] = True
+    if variant == "mha":
+        cfg.update(kv_heads=4, hidden=768, layers=3)
+    blob = gguf.synthetic_llama(cfg, seed=3, **kw)
+    prompt = gguf.prompt_tokens(7, cfg["vocab"], seed=1)
+    got, lg, again, ref, rlg = run_both(blob, prompt, 9)
+    assert_bits(lg, rlg)
+    assert got == ref and again == ref
+
+
+def test_tinyllama_config4_receipt():
+    cfg = gguf.TINYLLAMA
+    blob = gguf.synthetic_llama(cfg)
+    prompt = gguf.prompt_tokens(16, cfg["vocab"])
+    got, lg, again, ref, rlg = run_both(blob, prompt, 64)
+    assert_bits(lg, rlg)
+    assert got == ref == again
+    arch = gguf.arch_string(cfg)
+    r_gpu = receipt.decode_receipt(gguf.MODEL_ID, blob, arch, prompt, 64, got)
+    r_cpu = receipt.decode_receipt(gguf.MODEL_ID, blob, arch, prompt, 64, ref)
+    assert r_gpu == r_cpu
+
+
+def test_decode_errors():
+    blob = gguf.synthetic_llama(SMALL, seed=3)
+    with pytest.raises(vtq.Malformed):
+        vtq.DecodeSession(b"NOPE" + blob[4:])
+    with pytest.raises(vtq.Truncated):
+        vtq.DecodeSession(blob[: len(blob) // 2])
+    sess = vtq.DecodeSession(blob)
+    with pytest.raises(vtq.Internal, match="exceeds seq_len"):
+        sess.run([5] * 60, 10)
+    with pytest.raises(vtq.Internal, match="must not be empty"):
+        sess.run([], 3)
+    sess.close()

@@ -310,14 +310,30 @@ cudaError_t get_tensor_map(const DevMatrix& m, int box_x_u32, int box_y, CUtenso
     return cudaSuccess;
   }
   if (cache.size() > 4096) cache.clear();
+  // The driver entry point is resolved at run time so that the library loads
+  // (for ABI checks) on machines without a CUDA driver.
+  typedef CUresult (*EncodeFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                               const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                               const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                               CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+  static EncodeFn encode = nullptr;
+  if (!encode) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) !=
+            cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || !fn)
+      return cudaErrorInvalidValue;
+    encode = reinterpret_cast<EncodeFn>(fn);
+  }
   cuuint64_t gdim[2] = {(cuuint64_t)(m.pitch / 4), (cuuint64_t)m.out_feat};
   cuuint64_t gstride[1] = {(cuuint64_t)m.pitch};
   cuuint32_t box[2] = {(cuuint32_t)box_x_u32, (cuuint32_t)box_y};
   cuuint32_t estride[2] = {1, 1};
-  const CUresult r = cuTensorMapEncodeTiled(
-      out, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<uint8_t*>(m.data), gdim, gstride, box,
-      estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  const CUresult r = encode(out, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<uint8_t*>(m.data),
+                            gdim, gstride, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                            CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
   cache.emplace(key, *out);
   return cudaSuccess;

@@ -1,0 +1,777 @@
+// decode.cu -- the reference's quantized Llama decode step on the device.
+//
+// Mirrors src/model/forward_quantized.rs:329-649 (step_with_recorders, Llama
+// path) and the prompt + greedy loop of src/model/inference.rs:312-327, with
+// the weights resident in HBM and every linear on the sm_100a kernels
+// (kquant_matvec.cu / canon_matvec.cu). One decode step is captured once as a
+// CUDA graph; the position and the current token live in device memory and the
+// last kernel of a step selects the next token on the device, so a whole
+// prompt + generation is a sequence of graph launches with no host round trip.
+//
+// Order-pinned pieces (each a single thread or an exact parallel map):
+//   rms_norm       serial sum of squares over the row (rms_norm.rs:97-100)
+//   attention      serial q.k over head_dim, serial softmax sum, serial P.V
+//                  over positions (forward_quantized.rs:476-500, :925-941)
+//   RoPE           host tables from the restated powf/cosf/sinf (vtq_libm.h)
+//   SwiGLU/softmax expf restated on the device (vtq_libm.h)
+#include <cuda_fp16.h>
+
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <string>
+#include <vector>
+
+#include "../../include/vtq.h"
+#include "vtq_device.cuh"
+#include "vtq_internal.h"
+#include "vtq_libm.h"
+
+namespace vtq {
+
+cudaError_t launch_kq_or_canon(const DevMatrix& m, const float* x, float* y, unsigned* status,
+                               cudaStream_t st) {
+  if (m.dtype == T_Q4_K || m.dtype == T_Q6_K)
+    return launch_kq_matvec(m, x, m.in_feat, 1, y, m.out_feat, status, st);
+  return launch_canon_matvec(m, x, m.in_feat, 1, y, m.out_feat, status, st);
+}
+
+namespace {
+
+// ---------------------------------------------------------------- GGUF ----
+// Zero-copy parse of a GGUF v2/v3 blob (src/model/gguf.rs:305-422): metadata
+// scalars and strings, tensor infos, alignment, tensor byte ranges.
+struct GTensor {
+  std::vector<uint64_t> shape;
+  int dtype;
+  const uint8_t* bytes;
+  size_t len;
+};
+struct GMeta {
+  int type;
+  uint64_t u;  // unsigned / bool / signed as two's complement
+  double f;
+  std::string s;
+  uint64_t arr_len;
+};
+struct Gguf {
+  std::map<std::string, GMeta> meta;
+  std::map<std::string, GTensor> tensors;
+};
+
+struct GgufError {
+  vtq_status status;
+  const char* msg;
+};
+
+struct Cur {
+  const uint8_t* p;
+  size_t n, pos = 0;
+  const uint8_t* take(size_t k) {
+    if (k > n - pos) throw GgufError{VTQ_ERR_TRUNCATED, "gguf: read past end"};
+    const uint8_t* r = p + pos;
+    pos += k;
+    return r;
+  }
+  uint32_t u32() { uint32_t v; memcpy(&v, take(4), 4); return v; }
+  uint64_t u64() { uint64_t v; memcpy(&v, take(8), 8); return v; }
+  std::string str() {
+    const uint64_t k = u64();
+    if (k > (1u << 20)) throw GgufError{VTQ_ERR_MALFORMED, "gguf: string length > 1 MiB"};
+    const uint8_t* s = take((size_t)k);
+    return std::string(reinterpret_cast<const char*>(s), (size_t)k);
+  }
+};
+
+size_t value_size(int t) {
+  switch (t) {
+    case 0: case 1: case 7: return 1;
+    case 2: case 3: return 2;
+    case 4: case 5: case 6: return 4;
+    case 10: case 11: case 12: return 8;
+    default: return 0;
+  }
+}
+
+GMeta read_value(Cur& c, int t) {
+  GMeta m{};
+  m.type = t;
+  switch (t) {
+    case 0: m.u = *c.take(1); break;
+    case 1: m.u = (uint64_t)(int64_t)(int8_t)*c.take(1); break;
+    case 2: { uint16_t v; memcpy(&v, c.take(2), 2); m.u = v; break; }
+    case 3: { int16_t v; memcpy(&v, c.take(2), 2); m.u = (uint64_t)(int64_t)v; break; }
+    case 4: m.u = c.u32(); break;
+    case 5: m.u = (uint64_t)(int64_t)(int32_t)c.u32(); break;
+    case 6: { uint32_t b = c.u32(); float f; memcpy(&f, &b, 4); m.f = f; break; }
+    case 7: m.u = *c.take(1) != 0; break;
+    case 8: m.s = c.str(); break;
+    case 9: {
+      const int et = (int)c.u32();
+      if (et == 9) throw GgufError{VTQ_ERR_MALFORMED, "gguf: nested arrays not supported"};
+      if (et > 12) throw GgufError{VTQ_ERR_MALFORMED, "gguf: bad array elem type"};
+      m.arr_len = c.u64();
+      if (et == 8) {
+        for (uint64_t i = 0; i < m.arr_len; i++) c.str();
+      } else {
+        const unsigned __int128 total = (unsigned __int128)m.arr_len * value_size(et);
+        if (total > c.n) throw GgufError{VTQ_ERR_TRUNCATED, "gguf: array past end"};
+        c.take((size_t)total);
+      }
+      break;
+    }
+    case 10: m.u = c.u64(); break;
+    case 11: m.u = c.u64(); break;
+    case 12: { uint64_t b = c.u64(); memcpy(&m.f, &b, 8); break; }
+    default: throw GgufError{VTQ_ERR_MALFORMED, "gguf: unknown value type"};
+  }
+  return m;
+}
+
+Gguf parse_gguf(const uint8_t* blob, size_t len) {
+  Cur c{blob, len};
+  Gguf g;
+  if (memcmp(c.take(4), "GGUF", 4) != 0)
+    throw GgufError{VTQ_ERR_MALFORMED, "gguf: bad magic (not 'GGUF')"};
+  const uint32_t version = c.u32();
+  if (version != 2 && version != 3)
+    throw GgufError{VTQ_ERR_MALFORMED, "gguf: unsupported version (only v2/v3 supported)"};
+  const uint64_t nt = c.u64(), nm = c.u64();
+  for (uint64_t i = 0; i < nm; i++) {
+    std::string key = c.str();
+    g.meta[key] = read_value(c, (int)c.u32());
+  }
+  struct Info { std::string name; std::vector<uint64_t> shape; int dtype; uint64_t off; };
+  std::vector<Info> infos;
+  for (uint64_t i = 0; i < nt; i++) {
+    Info in;
+    in.name = c.str();
+    const uint32_t nd = c.u32();
+    if (nd > 8) throw GgufError{VTQ_ERR_MALFORMED, "gguf: tensor rank > 8 (sanity bound)"};
+    for (uint32_t d = 0; d < nd; d++) in.shape.push_back(c.u64());
+    in.dtype = (int)c.u32();
+    in.off = c.u64();
+    infos.push_back(in);
+  }
+  uint64_t align = 32;
+  auto it = g.meta.find("general.alignment");
+  if (it != g.meta.end() && it->second.type == 4) align = it->second.u;
+  if (align == 0) throw GgufError{VTQ_ERR_MALFORMED, "gguf: general.alignment is zero"};
+  const uint64_t base = (c.pos + align - 1) / align * align;
+  for (auto& in : infos) {
+    unsigned __int128 numel = 1;
+    for (uint64_t d : in.shape) {
+      numel *= d;
+      if (numel >> 64) throw GgufError{VTQ_ERR_MALFORMED, "gguf: shape product overflows u64"};
+    }
+    int64_t per, nb;
+    switch (in.dtype) {
+      case T_F32: per = 1; nb = 4; break;
+      case T_F16: per = 1; nb = 2; break;
+      case T_Q4_0: per = 32; nb = 18; break;
+      case T_Q5_0: per = 32; nb = 22; break;
+      case T_Q8_0: per = 32; nb = 34; break;
+      case T_Q4_K: per = 256; nb = 144; break;
+      case T_Q6_K: per = 256; nb = 210; break;
+      default:
+        throw GgufError{VTQ_ERR_MALFORMED, "gguf: byte size unknown for unsupported ggml_type"};
+    }
+    if ((uint64_t)numel % per)
+      throw GgufError{VTQ_ERR_MALFORMED, "gguf: tensor numel not a multiple of the block size"};
+    const unsigned __int128 bytes = (unsigned __int128)((uint64_t)numel / per) * nb;
+    const unsigned __int128 end = (unsigned __int128)base + in.off + bytes;
+    if (end > len) throw GgufError{VTQ_ERR_TRUNCATED, "gguf: tensor extends past end of file"};
+    g.tensors[in.name] = GTensor{in.shape, in.dtype, blob + base + in.off, (size_t)bytes};
+  }
+  return g;
+}
+
+// ------------------------------------------------------------- kernels ----
+
+constexpr uint32_t FULL = 0xffffffffu;
+
+struct StepState {  // device-resident per-run state
+  int pos;          // position of the step about to run
+  uint32_t cur;     // token fed at `pos`
+  int n_prompt, total, n_gen;
+};
+
+// embedding_row (forward_quantized.rs:818-919): dequantise one row of the
+// table into x. Device layouts as uploaded (Q6_K regrouped, see repack.cu).
+__global__ void embed_kernel(const uint8_t* table, int dtype, int64_t pitch, int dim,
+                             const StepState* st, float* x) {
+  const uint32_t row = st->cur;
+  const uint8_t* r = table + (int64_t)row * pitch;
+  for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < dim; e += gridDim.x * blockDim.x) {
+    float v;
+    if (dtype == T_F32) {
+      v = reinterpret_cast<const float*>(r)[e];
+    } else if (dtype == T_Q8_0) {
+      const uint8_t* b = r + (e >> 5) * 34;
+      v = __fmul_rn(f16_bits_to_f32(b[0] | (b[1] << 8)), (float)(int8_t)b[2 + (e & 31)]);
+    } else if (dtype == T_Q4_K) {  // quant.rs:280-326
+      const uint8_t* sb = r + (e >> 8) * 144;
+      const int k = e & 255, half = k >> 6, hi = (k >> 5) & 1, l = k & 31, j = 2 * half + hi;
+      const uint8_t* s = sb + 4;
+      int sc, m;
+      if (j < 4) {
+        sc = s[j] & 63;
+        m = s[j + 4] & 63;
+      } else {
+        sc = (s[j + 4] & 0x0F) | ((s[j - 4] >> 6) << 4);
+        m = (s[j + 4] >> 4) | ((s[j] >> 6) << 4);
+      }
+      const float d = f16_bits_to_f32(sb[0] | (sb[1] << 8));
+      const float dmin = f16_bits_to_f32(sb[2] | (sb[3] << 8));
+      const uint8_t byte = sb[16 + 32 * half + l];
+      const int q = hi ? (byte >> 4) : (byte & 15);
+      v = __fsub_rn(__fmul_rn(__fmul_rn(d, (float)sc), (float)q), __fmul_rn(dmin, (float)m));
+    } else {  // Q6_K, device layout: group of G superblocks
+      const int s = e >> 8, gi = s >> 3, i = s & 7;
+      const int S = dim >> 8, G = min(8, S - 8 * gi);
+      const uint8_t* gb = r + gi * 1680;
+      const int k = e & 255, half = k >> 7, w = k & 127, t = w >> 5, l = w & 31;
+      // ql byte (64 half + l + 32 (t & 1)), nibble t >> 1; qh byte (32 half + l), bits 2t.
+      const int qlb = 64 * half + l + 32 * (t & 1), qhb = 32 * half + l;
+      const uint8_t ql = gb[16 * (G * (qlb >> 4) + i) + (qlb & 15)];
+      const uint8_t qh = gb[128 * G + 16 * (G * (qhb >> 4) + i) + (qhb & 15)];
+      const int q = (int)(((t >> 1) ? (ql >> 4) : (ql & 15)) | (((qh >> (2 * t)) & 3) << 4)) - 32;
+      const int sc = (int8_t)gb[192 * G + 16 * i + 8 * half + (l >> 4) + 2 * t];
+      const float d = f16_bits_to_f32(gb[208 * G + 2 * i] | (gb[208 * G + 2 * i + 1] << 8));
+      v = __fmul_rn(__fmul_rn(d, (float)sc), (float)q);  // d * s * q (quant.rs:378-381)
+    }
+    x[e] = v;
+  }
+}
+
+// x = x + delta (if delta), then xb = rms_norm(x) * w (rms_norm.rs:94-108):
+// sumsq accumulated serially in element order by one thread.
+__global__ void rmsnorm_kernel(float* x, const float* delta, const float* w, float eps, int n,
+                               float* out) {
+  extern __shared__ float sq[];
+  __shared__ float s_scale;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    float v = x[i];
+    if (delta) {
+      v = __fadd_rn(v, delta[i]);
+      x[i] = v;
+    }
+    sq[i] = __fmul_rn(v, v);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float s = 0.0f;
+    for (int i = 0; i < n; i += 4) {
+      const float4 q = *reinterpret_cast<const float4*>(sq + i);
+      s = __fadd_rn(s, q.x);
+      if (i + 1 < n) s = __fadd_rn(s, q.y);
+      if (i + 2 < n) s = __fadd_rn(s, q.z);
+      if (i + 3 < n) s = __fadd_rn(s, q.w);
+    }
+    const float mean = __fdiv_rn(s, (float)n);
+    s_scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
+  }
+  __syncthreads();
+  const float scale = s_scale;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float v = x[i];
+    out[i] = __fmul_rn(__fmul_rn(v, scale), w[i]);
+  }
+}
+
+// Cache v and k at pos, then interleaved RoPE on q and the cached k
+// (forward_quantized.rs:407-472). rope tables: [seq_len][head_size / 2].
+__global__ void rope_kv_kernel(float* q, const float* k, const float* v, float* kc, float* vc,
+                               int layer, int seq_len, int dim, int kv_dim, int hs,
+                               const float* rcos, const float* rsin, const StepState* st) {
+  const int pos = st->pos;
+  const size_t off = ((size_t)layer * seq_len + pos) * kv_dim;
+  for (int p = blockIdx.x * blockDim.x + threadIdx.x; p < dim / 2;
+       p += gridDim.x * blockDim.x) {
+    const int i = 2 * p;
+    const int idx = i % hs;
+    const float fcr = rcos[(size_t)pos * (hs / 2) + idx / 2];
+    const float fci = rsin[(size_t)pos * (hs / 2) + idx / 2];
+    const float q0 = q[i], q1 = q[i + 1];
+    q[i] = __fsub_rn(__fmul_rn(q0, fcr), __fmul_rn(q1, fci));
+    q[i + 1] = __fadd_rn(__fmul_rn(q0, fci), __fmul_rn(q1, fcr));
+    if (i < kv_dim) {
+      const float k0 = k[i], k1 = k[i + 1];
+      kc[off + i] = __fsub_rn(__fmul_rn(k0, fcr), __fmul_rn(k1, fci));
+      kc[off + i + 1] = __fadd_rn(__fmul_rn(k0, fci), __fmul_rn(k1, fcr));
+      vc[off + i] = v[i];
+      vc[off + i + 1] = v[i + 1];
+    }
+  }
+}
+
+// One CTA per head (forward_quantized.rs:476-500, softmax :925-941).
+__global__ void attention_kernel(const float* q, const float* kc, const float* vc, int layer,
+                                 int seq_len, int kv_dim, int hs, int kv_mul, const StepState* st,
+                                 float* out) {
+  extern __shared__ float sm[];
+  float* qh = sm;        // [hs]
+  float* att = sm + hs;  // [pos + 1]
+  __shared__ float s_max, s_inv;
+  const int h = blockIdx.x, pos = st->pos, np = pos + 1;
+  const float* kbase = kc + (size_t)layer * seq_len * kv_dim + (h / kv_mul) * hs;
+  const float* vbase = vc + (size_t)layer * seq_len * kv_dim + (h / kv_mul) * hs;
+  for (int d = threadIdx.x; d < hs; d += blockDim.x) qh[d] = q[h * hs + d];
+  __syncthreads();
+  const float root = __fsqrt_rn((float)hs);
+  for (int t = threadIdx.x; t < np; t += blockDim.x) {
+    const float* kt = kbase + (size_t)t * kv_dim;
+    float score = 0.0f;
+    for (int d = 0; d < hs; d++) score = __fadd_rn(score, __fmul_rn(qh[d], kt[d]));
+    att[t] = __fdiv_rn(score, root);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float mx = -INFINITY;
+    for (int t = 0; t < np; t++)
+      if (att[t] > mx) mx = att[t];
+    s_max = mx;
+  }
+  __syncthreads();
+  for (int t = threadIdx.x; t < np; t += blockDim.x) att[t] = libm::expf(__fsub_rn(att[t], s_max));
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float sum = 0.0f;
+    for (int t = 0; t < np; t++) sum = __fadd_rn(sum, att[t]);
+    s_inv = __fdiv_rn(1.0f, sum);
+  }
+  __syncthreads();
+  for (int t = threadIdx.x; t < np; t += blockDim.x) att[t] = __fmul_rn(att[t], s_inv);
+  __syncthreads();
+  for (int d = threadIdx.x; d < hs; d += blockDim.x) {
+    float acc = 0.0f;
+    for (int t = 0; t < np; t++)
+      acc = __fadd_rn(acc, __fmul_rn(att[t], vbase[(size_t)t * kv_dim + d]));
+    out[h * hs + d] = acc;
+  }
+}
+
+// SwiGLU: silu(g) * up with silu = g / (1 + expf(-g)) (forward_quantized.rs:556-561).
+__global__ void swiglu_kernel(const float* g, const float* u, float* out, int n) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const float gi = g[i];
+    const float silu = __fdiv_rn(gi, __fadd_rn(1.0f, libm::expf(-gi)));
+    out[i] = __fmul_rn(silu, u[i]);
+  }
+}
+
+// argmax (argmax.rs:49-60: first index of the maximum, strict >) and the
+// token choice of the run loop (inference.rs:318-326), then pos += 1.
+__global__ void argmax_next_kernel(const float* logits, int n, StepState* st,
+                                   const uint32_t* prompt, uint32_t* out_tokens) {
+  __shared__ float bv[32];
+  __shared__ int bi[32];
+  float best = -INFINITY;
+  int besti = 0x7fffffff;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float v = logits[i];
+    if (v > best || (v == best && i < besti)) {
+      best = v;
+      besti = i;
+    }
+  }
+  for (int o = 16; o; o >>= 1) {
+    const float ov = __shfl_down_sync(FULL, best, o);
+    const int oi = __shfl_down_sync(FULL, besti, o);
+    if (ov > best || (ov == best && oi < besti)) {
+      best = ov;
+      besti = oi;
+    }
+  }
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) {
+    bv[w] = best;
+    bi[w] = besti;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int k = 1; k < (int)(blockDim.x >> 5); k++)
+      if (bv[k] > best || (bv[k] == best && bi[k] < besti)) {
+        best = bv[k];
+        besti = bi[k];
+      }
+    // NaN at index 0 is never beaten by a strict > (sequential rule).
+    if (logits[0] != logits[0] || besti == 0x7fffffff) besti = 0;
+    const int pos = st->pos;
+    const uint32_t picked = (uint32_t)besti;
+    const uint32_t next = (pos + 1 < st->n_prompt) ? prompt[pos + 1] : picked;
+    if (pos >= st->n_prompt) out_tokens[st->n_gen++] = next;
+    st->cur = next;
+    st->pos = pos + 1;
+  }
+}
+
+// Copy the step's logits into the per-position log (optional output).
+__global__ void log_logits_kernel(const float* logits, int vocab, const StepState* st,
+                                  float* log) {
+  const int pos = st->pos;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < vocab; i += gridDim.x * blockDim.x)
+    log[(size_t)pos * vocab + i] = logits[i];
+}
+
+}  // namespace
+}  // namespace vtq
+
+using namespace vtq;
+
+struct vtq_decode {
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  int dim = 0, hidden = 0, n_layers = 0, n_heads = 0, n_kv_heads = 0, vocab = 0, seq_len = 0;
+  bool shared = false;
+  float rope_theta = 10000.0f, rms_eps = 1e-5f;
+  std::vector<void*> allocs;
+  DevMatrix embd{}, head{};
+  struct Layer {
+    float *rms_att, *rms_ffn;
+    DevMatrix wq, wk, wv, wo, w1, w2, w3;
+  };
+  std::vector<Layer> layers;
+  float* rms_final = nullptr;
+  float *rcos = nullptr, *rsin = nullptr, *kc = nullptr, *vc = nullptr;
+  float *x, *xb, *q, *k, *v, *xo, *xb2, *g, *u, *inner, *logits;
+  float* logit_log = nullptr;
+  size_t logit_log_cap = 0;
+  StepState* st = nullptr;
+  uint32_t* prompt = nullptr;
+  uint32_t* out_tokens = nullptr;
+  unsigned* status = nullptr;
+  cudaGraphExec_t graph = nullptr;
+  bool graph_logs = false;
+  std::string err;
+};
+
+namespace {
+
+vtq_status dfail(vtq_decode* d, vtq_status s, const std::string& m) {
+  if (d) d->err = m;
+  return s;
+}
+
+#define DCUDA(d, call)                                                                   \
+  do {                                                                                   \
+    cudaError_t e_ = (call);                                                             \
+    if (e_ != cudaSuccess)                                                               \
+      return dfail((d), e_ == cudaErrorMemoryAllocation ? VTQ_ERR_OOM : VTQ_ERR_GPU,     \
+                   std::string("gpu error: ") + #call + ": " + cudaGetErrorString(e_)); \
+  } while (0)
+
+template <typename T>
+vtq_status dalloc(vtq_decode* d, T** p, size_t bytes) {
+  void* q = nullptr;
+  DCUDA(d, cudaMalloc(&q, bytes ? bytes : 16));
+  d->allocs.push_back(q);
+  *p = static_cast<T*>(q);
+  return VTQ_OK;
+}
+
+vtq_status upload_matrix(vtq_decode* d, const GTensor& t, int64_t in, int64_t out, DevMatrix* m) {
+  if (t.shape.size() != 2 || (int64_t)t.shape[0] != in || (int64_t)t.shape[1] != out)
+    return dfail(d, VTQ_ERR_INTERNAL, "gguf: weight shape mismatch");
+  const int64_t rb = packed_row_bytes(t.dtype, in);
+  if (rb < 0) return dfail(d, VTQ_ERR_NOT_IMPLEMENTED, "weight dtype not supported by the kernels");
+  m->dtype = t.dtype;
+  m->in_feat = in;
+  m->out_feat = out;
+  m->row_bytes = rb;
+  m->pitch = device_pitch(t.dtype, in);
+  uint8_t *dst, *stage;
+  if (vtq_status s = dalloc(d, &dst, (size_t)(out * m->pitch + 16))) return s;
+  DCUDA(d, cudaMalloc(&stage, t.len));
+  DCUDA(d, cudaMemcpy(stage, t.bytes, t.len, cudaMemcpyHostToDevice));
+  DCUDA(d, launch_repack(stage, *m, dst, d->stream));
+  DCUDA(d, cudaMemsetAsync(dst + out * m->pitch, 0, 16, d->stream));
+  DCUDA(d, cudaStreamSynchronize(d->stream));
+  cudaFree(stage);
+  m->data = dst;
+  return VTQ_OK;
+}
+
+vtq_status upload_f32(vtq_decode* d, const Gguf& g, const std::string& name, int n, float** out) {
+  auto it = g.tensors.find(name);
+  if (it == g.tensors.end())
+    return dfail(d, VTQ_ERR_INTERNAL, "gguf: required Llama tensor not found: " + name);
+  if (it->second.dtype != T_F32)
+    return dfail(d, VTQ_ERR_INTERNAL, "gguf: expected F32 norm-weight tensor, got something else");
+  if ((int64_t)it->second.len != (int64_t)n * 4)
+    return dfail(d, VTQ_ERR_INTERNAL, "gguf: norm length mismatch");
+  if (vtq_status s = dalloc(d, out, (size_t)n * 4)) return s;
+  DCUDA(d, cudaMemcpy(*out, it->second.bytes, (size_t)n * 4, cudaMemcpyHostToDevice));
+  return VTQ_OK;
+}
+
+const GTensor* need(vtq_decode* d, const Gguf& g, const std::string& name) {
+  auto it = g.tensors.find(name);
+  if (it == g.tensors.end()) {
+    d->err = "gguf: required Llama tensor not found: " + name;
+    return nullptr;
+  }
+  return &it->second;
+}
+
+int64_t meta_uint(const Gguf& g, const std::string& key, bool* ok) {
+  auto it = g.meta.find(key);
+  if (it == g.meta.end()) {
+    *ok = false;
+    return 0;
+  }
+  const GMeta& m = it->second;
+  switch (m.type) {
+    case 4: case 10: return (int64_t)m.u;
+    case 5: case 11: if ((int64_t)m.u >= 0) return (int64_t)m.u; break;
+    default: break;
+  }
+  *ok = false;
+  return 0;
+}
+
+// One decode step: every launch on d->stream; captured into the graph.
+vtq_status enqueue_step(vtq_decode* d, bool log_logits) {
+  cudaStream_t s = d->stream;
+  const int dim = d->dim, hs = dim / d->n_heads, kv_dim = d->n_kv_heads * hs;
+  const int kv_mul = d->n_heads / d->n_kv_heads;
+  embed_kernel<<<(dim + 255) / 256, 256, 0, s>>>(d->embd.data, d->embd.dtype, d->embd.pitch, dim,
+                                                  d->st, d->x);
+  const size_t rms_smem = ((size_t)dim + 4) * 4;
+  const float* delta = nullptr;
+  for (int l = 0; l < d->n_layers; l++) {
+    auto& L = d->layers[l];
+    rmsnorm_kernel<<<1, 1024, rms_smem, s>>>(d->x, delta, L.rms_att, d->rms_eps, dim, d->xb);
+    DCUDA(d, launch_kq_or_canon(L.wq, d->xb, d->q, d->status, s));
+    DCUDA(d, launch_kq_or_canon(L.wk, d->xb, d->k, d->status, s));
+    DCUDA(d, launch_kq_or_canon(L.wv, d->xb, d->v, d->status, s));
+    rope_kv_kernel<<<(dim / 2 + 255) / 256, 256, 0, s>>>(d->q, d->k, d->v, d->kc, d->vc, l,
+                                                        d->seq_len, dim, kv_dim, hs, d->rcos,
+                                                        d->rsin, d->st);
+    attention_kernel<<<d->n_heads, 128, ((size_t)hs + d->seq_len) * 4, s>>>(
+        d->q, d->kc, d->vc, l, d->seq_len, kv_dim, hs, kv_mul, d->st, d->xo);
+    DCUDA(d, launch_kq_or_canon(L.wo, d->xo, d->xb2, d->status, s));
+    rmsnorm_kernel<<<1, 1024, rms_smem, s>>>(d->x, d->xb2, L.rms_ffn, d->rms_eps, dim, d->xb);
+    DCUDA(d, launch_kq_or_canon(L.w1, d->xb, d->g, d->status, s));
+    DCUDA(d, launch_kq_or_canon(L.w3, d->xb, d->u, d->status, s));
+    swiglu_kernel<<<(d->hidden + 255) / 256, 256, 0, s>>>(d->g, d->u, d->inner, d->hidden);
+    DCUDA(d, launch_kq_or_canon(L.w2, d->inner, d->xb2, d->status, s));
+    delta = d->xb2;
+  }
+  rmsnorm_kernel<<<1, 1024, rms_smem, s>>>(d->x, delta, d->rms_final, d->rms_eps, dim, d->xb);
+  DCUDA(d, launch_kq_or_canon(d->head, d->xb, d->logits, d->status, s));
+  if (log_logits)
+    log_logits_kernel<<<(d->vocab + 255) / 256, 256, 0, s>>>(d->logits, d->vocab, d->st,
+                                                              d->logit_log);
+  argmax_next_kernel<<<1, 1024, 0, s>>>(d->logits, d->vocab, d->st, d->prompt, d->out_tokens);
+  DCUDA(d, cudaGetLastError());
+  return VTQ_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+vtq_status vtq_decode_open(vtq_ctx* ctx, int device, const uint8_t* gguf, size_t len,
+                           vtq_decode** out) {
+  if (!out || !gguf) return VTQ_ERR_INVALID_ARG;
+  *out = nullptr;
+  (void)ctx;
+  auto* d = new vtq_decode();
+  d->device = device;
+  vtq_status s = VTQ_OK;
+  cudaError_t ce = cudaSetDevice(device);
+  if (ce == cudaSuccess) ce = cudaStreamCreateWithFlags(&d->stream, cudaStreamNonBlocking);
+  if (ce != cudaSuccess) {
+    delete d;
+    return VTQ_ERR_GPU;
+  }
+  *out = d;
+  Gguf g;
+  try {
+    g = parse_gguf(gguf, len);
+  } catch (const GgufError& e) {
+    d->err = e.msg;
+    return e.status;
+  }
+  // Config (src/model/config.rs:156-212) and Llama hyperparameters (quant_weights.rs:137-151).
+  auto arch_it = g.meta.find("general.architecture");
+  if (arch_it == g.meta.end() || arch_it->second.type != 8)
+    return dfail(d, VTQ_ERR_INTERNAL, "gguf: missing 'general.architecture' metadata");
+  const std::string arch = arch_it->second.s;
+  if (arch != "llama")
+    return dfail(d, VTQ_ERR_NOT_IMPLEMENTED, "decode session: only the llama architecture");
+  bool ok = true;
+  d->dim = (int)meta_uint(g, arch + ".embedding_length", &ok);
+  d->hidden = (int)meta_uint(g, arch + ".feed_forward_length", &ok);
+  d->n_layers = (int)meta_uint(g, arch + ".block_count", &ok);
+  d->n_heads = (int)meta_uint(g, arch + ".attention.head_count", &ok);
+  d->seq_len = (int)meta_uint(g, arch + ".context_length", &ok);
+  bool ok_kv = true;
+  d->n_kv_heads = (int)meta_uint(g, arch + ".attention.head_count_kv", &ok_kv);
+  if (!ok_kv) d->n_kv_heads = d->n_heads;
+  auto tok = g.meta.find("tokenizer.ggml.tokens");
+  if (tok != g.meta.end() && tok->second.type == 9)
+    d->vocab = (int)tok->second.arr_len;
+  else
+    d->vocab = (int)meta_uint(g, arch + ".vocab_size", &ok);
+  if (!ok) return dfail(d, VTQ_ERR_INTERNAL, "gguf: numeric metadata missing or wrong type");
+  auto f32meta = [&](const std::string& key, float def) {
+    auto it = g.meta.find(key);
+    return (it != g.meta.end() && it->second.type == 6) ? (float)it->second.f : def;
+  };
+  d->rope_theta = f32meta(arch + ".rope.freq_base", 10000.0f);
+  d->rms_eps = f32meta(arch + ".attention.layer_norm_rms_epsilon", 1e-5f);
+  if (d->dim <= 0 || d->n_heads <= 0 || d->dim % d->n_heads || d->n_kv_heads <= 0 ||
+      d->n_heads % d->n_kv_heads || (d->dim / d->n_heads) % 2 || d->dim > 8192 ||
+      d->seq_len <= 0 || d->vocab <= 0)
+    return dfail(d, VTQ_ERR_INTERNAL, "decode session: unsupported model shape");
+  const int dim = d->dim, hs = dim / d->n_heads, kv_dim = d->n_kv_heads * hs;
+  const GTensor* te = need(d, g, "token_embd.weight");
+  if (!te) return VTQ_ERR_INTERNAL;
+  if ((s = upload_matrix(d, *te, dim, d->vocab, &d->embd))) return s;
+  auto wcls = g.tensors.find("output.weight");
+  d->shared = wcls == g.tensors.end();
+  if (d->shared)
+    d->head = d->embd;
+  else if ((s = upload_matrix(d, wcls->second, dim, d->vocab, &d->head)))
+    return s;
+  if ((s = upload_f32(d, g, "output_norm.weight", dim, &d->rms_final))) return s;
+  d->layers.resize(d->n_layers);
+  for (int l = 0; l < d->n_layers; l++) {
+    auto& L = d->layers[l];
+    const std::string p = "blk." + std::to_string(l) + ".";
+    if ((s = upload_f32(d, g, p + "attn_norm.weight", dim, &L.rms_att))) return s;
+    if ((s = upload_f32(d, g, p + "ffn_norm.weight", dim, &L.rms_ffn))) return s;
+    if (g.tensors.count(p + "attn_q.bias"))
+      return dfail(d, VTQ_ERR_NOT_IMPLEMENTED, "decode session: QKV bias (Qwen2) not supported");
+    struct {
+      const char* name;
+      int64_t in, out;
+      DevMatrix* m;
+    } mats[] = {{"attn_q.weight", dim, dim, &L.wq},         {"attn_k.weight", dim, kv_dim, &L.wk},
+                {"attn_v.weight", dim, kv_dim, &L.wv},      {"attn_output.weight", dim, dim, &L.wo},
+                {"ffn_gate.weight", dim, d->hidden, &L.w1}, {"ffn_down.weight", d->hidden, dim, &L.w2},
+                {"ffn_up.weight", dim, d->hidden, &L.w3}};
+    for (auto& mm : mats) {
+      const GTensor* t = need(d, g, p + mm.name);
+      if (!t) return VTQ_ERR_INTERNAL;
+      if ((s = upload_matrix(d, *t, mm.in, mm.out, mm.m))) return s;
+    }
+  }
+  // RoPE tables from the restated libm (forward_quantized.rs:449-458).
+  std::vector<float> hc((size_t)d->seq_len * (hs / 2)), hsn((size_t)d->seq_len * (hs / 2));
+  for (int pos = 0; pos < d->seq_len; pos++)
+    for (int j = 0; j < hs / 2; j++) {
+      const int idx = 2 * j;
+      const float freq = 1.0f / libm::powf(d->rope_theta, (float)idx / (float)hs);
+      const float val = (float)pos * freq;
+      hc[(size_t)pos * (hs / 2) + j] = libm::cosf(val);
+      hsn[(size_t)pos * (hs / 2) + j] = libm::sinf(val);
+    }
+  if ((s = dalloc(d, &d->rcos, hc.size() * 4)) || (s = dalloc(d, &d->rsin, hsn.size() * 4)))
+    return s;
+  DCUDA(d, cudaMemcpy(d->rcos, hc.data(), hc.size() * 4, cudaMemcpyHostToDevice));
+  DCUDA(d, cudaMemcpy(d->rsin, hsn.data(), hsn.size() * 4, cudaMemcpyHostToDevice));
+  const size_t kvb = (size_t)d->n_layers * d->seq_len * kv_dim * 4;
+  if ((s = dalloc(d, &d->kc, kvb)) || (s = dalloc(d, &d->vc, kvb))) return s;
+  DCUDA(d, cudaMemset(d->kc, 0, kvb));
+  DCUDA(d, cudaMemset(d->vc, 0, kvb));
+  float** bufs[] = {&d->x, &d->xb, &d->q, &d->xo, &d->xb2};
+  for (float** b : bufs)
+    if ((s = dalloc(d, b, (size_t)dim * 4))) return s;
+  if ((s = dalloc(d, &d->k, (size_t)kv_dim * 4)) || (s = dalloc(d, &d->v, (size_t)kv_dim * 4)) ||
+      (s = dalloc(d, &d->g, (size_t)d->hidden * 4)) ||
+      (s = dalloc(d, &d->u, (size_t)d->hidden * 4)) ||
+      (s = dalloc(d, &d->inner, (size_t)d->hidden * 4)) ||
+      (s = dalloc(d, &d->logits, (size_t)d->vocab * 4)) ||
+      (s = dalloc(d, &d->st, sizeof(StepState))) ||
+      (s = dalloc(d, &d->prompt, (size_t)d->seq_len * 4)) ||
+      (s = dalloc(d, &d->out_tokens, (size_t)d->seq_len * 4)) || (s = dalloc(d, &d->status, 16)))
+    return s;
+  DCUDA(d, cudaMemset(d->status, 0, 16));
+  return VTQ_OK;
+}
+
+const char* vtq_decode_last_error(const vtq_decode* d) { return d ? d->err.c_str() : "null"; }
+
+vtq_status vtq_decode_config(const vtq_decode* d, int64_t* out8) {
+  if (!d || !out8) return VTQ_ERR_INVALID_ARG;
+  const int64_t v[8] = {d->dim,        d->hidden, d->n_layers, d->n_heads,
+                        d->n_kv_heads, d->vocab,  d->seq_len,  d->shared ? 1 : 0};
+  memcpy(out8, v, sizeof v);
+  return VTQ_OK;
+}
+
+vtq_status vtq_decode_run(vtq_decode* d, const uint32_t* prompt, size_t n_prompt, size_t n_new,
+                          uint32_t* out_tokens, float* logits) {
+  if (!d || (!prompt && n_prompt) || (!out_tokens && n_new)) return VTQ_ERR_INVALID_ARG;
+  if (n_prompt == 0)
+    return dfail(d, VTQ_ERR_INTERNAL, "invalid shape: prompt_tokens must not be empty");
+  const size_t total = n_prompt + n_new;
+  if (total > (size_t)d->seq_len)
+    return dfail(d, VTQ_ERR_INTERNAL, "invalid shape: prompt + n_new_tokens exceeds seq_len");
+  for (size_t i = 0; i < n_prompt; i++)
+    if (prompt[i] >= (uint32_t)d->vocab)
+      return dfail(d, VTQ_ERR_INTERNAL, "embedding_row: table too small for token id");
+  DCUDA(d, cudaSetDevice(d->device));
+  const bool want_logits = logits != nullptr;
+  if (want_logits && d->logit_log_cap < total * d->vocab) {
+    float* p;
+    if (vtq_status s = dalloc(d, &p, total * d->vocab * 4)) return s;
+    d->logit_log = p;
+    d->logit_log_cap = total * d->vocab;
+    if (d->graph) {
+      cudaGraphExecDestroy(d->graph);
+      d->graph = nullptr;
+    }
+  }
+  if (!d->graph || d->graph_logs != want_logits) {
+    if (d->graph) cudaGraphExecDestroy(d->graph);
+    d->graph = nullptr;
+    // One uncaptured step on a dummy state first: kernel attributes and tensor
+    // maps are set up outside the capture. (It writes position 0 of the KV
+    // cache, which every run rewrites before reading.)
+    StepState warm{0, 0u, 1, 1, 0};
+    DCUDA(d, cudaMemcpyAsync(d->st, &warm, sizeof warm, cudaMemcpyHostToDevice, d->stream));
+    if (vtq_status s0 = enqueue_step(d, want_logits)) return s0;
+    DCUDA(d, cudaStreamSynchronize(d->stream));
+    cudaGraph_t graph;
+    DCUDA(d, cudaStreamBeginCapture(d->stream, cudaStreamCaptureModeThreadLocal));
+    const vtq_status s = enqueue_step(d, want_logits);
+    cudaError_t ce = cudaStreamEndCapture(d->stream, &graph);
+    if (s) return s;
+    DCUDA(d, ce);
+    DCUDA(d, cudaGraphInstantiate(&d->graph, graph, 0));
+    cudaGraphDestroy(graph);
+    d->graph_logs = want_logits;
+  }
+  StepState hs{0, prompt[0], (int)n_prompt, (int)total, 0};
+  DCUDA(d, cudaMemcpyAsync(d->st, &hs, sizeof hs, cudaMemcpyHostToDevice, d->stream));
+  DCUDA(d, cudaMemcpyAsync(d->prompt, prompt, n_prompt * 4, cudaMemcpyHostToDevice, d->stream));
+  for (size_t pos = 0; pos < total; pos++) DCUDA(d, cudaGraphLaunch(d->graph, d->stream));
+  if (n_new)
+    DCUDA(d, cudaMemcpyAsync(out_tokens, d->out_tokens, n_new * 4, cudaMemcpyDeviceToHost,
+                             d->stream));
+  if (want_logits)
+    DCUDA(d, cudaMemcpyAsync(logits, d->logit_log, total * d->vocab * 4, cudaMemcpyDeviceToHost,
+                             d->stream));
+  unsigned stat = 0;
+  DCUDA(d, cudaMemcpyAsync(&stat, d->status, 4, cudaMemcpyDeviceToHost, d->stream));
+  DCUDA(d, cudaStreamSynchronize(d->stream));
+  if (stat) return dfail(d, VTQ_ERR_TIMEOUT, "decode: a device-side wait timed out");
+  return VTQ_OK;
+}
+
+vtq_status vtq_decode_close(vtq_decode* d) {
+  if (!d) return VTQ_ERR_INVALID_ARG;
+  cudaSetDevice(d->device);
+  if (d->stream) cudaStreamSynchronize(d->stream);
+  if (d->graph) cudaGraphExecDestroy(d->graph);
+  for (void* p : d->allocs) cudaFree(p);
+  if (d->stream) cudaStreamDestroy(d->stream);
+  delete d;
+  return VTQ_OK;
+}
+
+}  // extern "C"

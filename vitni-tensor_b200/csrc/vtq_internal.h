@@ -40,6 +40,10 @@ cudaError_t launch_kq_matvec(const DevMatrix& m, const float* x, int64_t ldx, in
 cudaError_t launch_canon_matvec(const DevMatrix& m, const float* x, int64_t ldx, int64_t batch,
                                 float* y, int64_t ldy, unsigned* status, cudaStream_t st);
 
+// The linear_dispatch arm for m's dtype (integer k-quant or canonical), batch 1.
+cudaError_t launch_kq_or_canon(const DevMatrix& m, const float* x, float* y, unsigned* status,
+                               cudaStream_t st);
+
 int num_sms();
 int max_smem_optin();
 

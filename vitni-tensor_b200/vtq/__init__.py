@@ -35,7 +35,9 @@ EXPORTS = (
     "vtq_weight_upload", "vtq_weight_free", "vtq_weight_info", "vtq_linear",
     "vtq_linear_dispatch", "vtq_linear_q4_k_integer", "vtq_linear_q6_k_integer",
     "vtq_linear_q4_k_fused", "vtq_linear_q4_0", "vtq_device_layout_bytes",
-    "vtq_device_repack", "vtq_linear_device",
+    "vtq_device_repack", "vtq_linear_device", "vtq_decode_open", "vtq_decode_last_error",
+    "vtq_decode_config", "vtq_decode_run", "vtq_decode_close", "vtq_expf", "vtq_sinf",
+    "vtq_cosf", "vtq_powf", "vtq_libm_sweep",
 )
 
 
@@ -114,6 +116,16 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         "vtq_device_repack": (c_i32, [c_i32, c_i64, c_i64, c_p, c_p, c_p]),
         "vtq_linear_device": (c_i32, [c_i32, c_p, c_i64, c_i64, c_p, c_i64, c_p, c_i64, c_i64,
                                       c_u32, c_p, c_p]),
+        "vtq_decode_open": (c_i32, [c_p, ctypes.c_int, c_p, c_sz, ctypes.POINTER(c_p)]),
+        "vtq_decode_last_error": (ctypes.c_char_p, [c_p]),
+        "vtq_decode_config": (c_i32, [c_p, c_p]),
+        "vtq_decode_run": (c_i32, [c_p, c_p, c_sz, c_sz, c_p, c_p]),
+        "vtq_decode_close": (c_i32, [c_p]),
+        "vtq_expf": (ctypes.c_float, [ctypes.c_float]),
+        "vtq_sinf": (ctypes.c_float, [ctypes.c_float]),
+        "vtq_cosf": (ctypes.c_float, [ctypes.c_float]),
+        "vtq_powf": (ctypes.c_float, [ctypes.c_float, ctypes.c_float]),
+        "vtq_libm_sweep": (None, [c_p, c_sz, c_p]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -259,6 +271,49 @@ def linear_dispatch(ctx: Context, x, w: QuantTensor, in_feat: int, out_feat: int
                                            in_feat, out_feat, _ptr(y),
                                            Q4K_FLOAT if q4k_float else 0))
     return y
+
+
+class DecodeSession:
+    """A GGUF Llama model resident on one GPU, decoded by run_quantized's loop
+    (src/model/inference.rs:274-345) with every step on the device."""
+
+    def __init__(self, gguf_blob: bytes, device: int = 0):
+        self.lib = load_library()
+        self._blob = np.frombuffer(bytes(gguf_blob), np.uint8)
+        h = ctypes.c_void_p()
+        st = self.lib.vtq_decode_open(None, device, _ptr(self._blob), self._blob.nbytes,
+                                      ctypes.byref(h))
+        self.handle = h.value
+        if st != OK:
+            msg = self.lib.vtq_decode_last_error(self.handle).decode() if self.handle else ""
+            self.close()
+            raise _ERRORS.get(st, Error)(msg)
+        cfg = np.zeros(8, np.int64)
+        self.lib.vtq_decode_config(self.handle, _ptr(cfg))
+        keys = ("dim", "hidden", "layers", "heads", "kv_heads", "vocab", "seq_len", "shared")
+        self.config = {k: int(v) for k, v in zip(keys, cfg)}
+
+    def run(self, prompt, n_new: int, logits: bool = False):
+        """Returns (generated token ids, per-step logits [n_prompt + n_new, vocab] or None)."""
+        p = np.ascontiguousarray(prompt, dtype=np.uint32)
+        out = np.zeros(max(1, n_new), np.uint32)
+        lg = np.zeros((len(p) + n_new, self.config["vocab"]), np.float32) if logits else None
+        st = self.lib.vtq_decode_run(self.handle, _ptr(p), len(p), n_new, _ptr(out),
+                                     _ptr(lg) if lg is not None else None)
+        if st != OK:
+            raise _ERRORS.get(st, Error)(self.lib.vtq_decode_last_error(self.handle).decode())
+        return out[:n_new].tolist(), lg
+
+    def close(self):
+        if getattr(self, "handle", None):
+            self.lib.vtq_decode_close(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 def device_layout_bytes(dtype: int, in_feat: int, rows: int) -> int:
