@@ -483,7 +483,7 @@ vtq_status upload_matrix(vtq_decode* d, const GTensor& t, int64_t in, int64_t ou
   uint8_t *dst, *stage;
   if (vtq_status s = dalloc(d, &dst, (size_t)(out * m->pitch + 16))) return s;
   DCUDA(d, cudaMalloc(&stage, t.len));
-  DCUDA(d, cudaMemcpy(stage, t.bytes, t.len, cudaMemcpyHostToDevice));
+  DCUDA(d, cudaMemcpyAsync(stage, t.bytes, t.len, cudaMemcpyHostToDevice, d->stream));
   DCUDA(d, launch_repack(stage, *m, dst, d->stream));
   DCUDA(d, cudaMemsetAsync(dst + out * m->pitch, 0, 16, d->stream));
   DCUDA(d, cudaStreamSynchronize(d->stream));
@@ -501,7 +501,9 @@ vtq_status upload_f32(vtq_decode* d, const Gguf& g, const std::string& name, int
   if ((int64_t)it->second.len != (int64_t)n * 4)
     return dfail(d, VTQ_ERR_INTERNAL, "gguf: norm length mismatch");
   if (vtq_status s = dalloc(d, out, (size_t)n * 4)) return s;
-  DCUDA(d, cudaMemcpy(*out, it->second.bytes, (size_t)n * 4, cudaMemcpyHostToDevice));
+  DCUDA(d, cudaMemcpyAsync(*out, it->second.bytes, (size_t)n * 4, cudaMemcpyHostToDevice,
+                           d->stream));
+  DCUDA(d, cudaStreamSynchronize(d->stream));
   return VTQ_OK;
 }
 
@@ -671,12 +673,17 @@ vtq_status vtq_decode_open(vtq_ctx* ctx, int device, const uint8_t* gguf, size_t
     }
   if ((s = dalloc(d, &d->rcos, hc.size() * 4)) || (s = dalloc(d, &d->rsin, hsn.size() * 4)))
     return s;
-  DCUDA(d, cudaMemcpy(d->rcos, hc.data(), hc.size() * 4, cudaMemcpyHostToDevice));
-  DCUDA(d, cudaMemcpy(d->rsin, hsn.data(), hsn.size() * 4, cudaMemcpyHostToDevice));
+  DCUDA(d, cudaMemcpyAsync(d->rcos, hc.data(), hc.size() * 4, cudaMemcpyHostToDevice, d->stream));
+  DCUDA(d, cudaMemcpyAsync(d->rsin, hsn.data(), hsn.size() * 4, cudaMemcpyHostToDevice,
+                           d->stream));
+  DCUDA(d, cudaStreamSynchronize(d->stream));
   const size_t kvb = (size_t)d->n_layers * d->seq_len * kv_dim * 4;
   if ((s = dalloc(d, &d->kc, kvb)) || (s = dalloc(d, &d->vc, kvb))) return s;
-  DCUDA(d, cudaMemset(d->kc, 0, kvb));
-  DCUDA(d, cudaMemset(d->vc, 0, kvb));
+  // All set-up work goes on the session stream: it is non-blocking, so work
+  // on the legacy default stream (a plain cudaMemset) would not be ordered
+  // before the first decode step.
+  DCUDA(d, cudaMemsetAsync(d->kc, 0, kvb, d->stream));
+  DCUDA(d, cudaMemsetAsync(d->vc, 0, kvb, d->stream));
   float** bufs[] = {&d->x, &d->xb, &d->q, &d->xo, &d->xb2};
   for (float** b : bufs)
     if ((s = dalloc(d, b, (size_t)dim * 4))) return s;
@@ -689,7 +696,8 @@ vtq_status vtq_decode_open(vtq_ctx* ctx, int device, const uint8_t* gguf, size_t
       (s = dalloc(d, &d->prompt, (size_t)d->seq_len * 4)) ||
       (s = dalloc(d, &d->out_tokens, (size_t)d->seq_len * 4)) || (s = dalloc(d, &d->status, 16)))
     return s;
-  DCUDA(d, cudaMemset(d->status, 0, 16));
+  DCUDA(d, cudaMemsetAsync(d->status, 0, 16, d->stream));
+  DCUDA(d, cudaStreamSynchronize(d->stream));
   return VTQ_OK;
 }
 
@@ -760,6 +768,18 @@ vtq_status vtq_decode_run(vtq_decode* d, const uint32_t* prompt, size_t n_prompt
   DCUDA(d, cudaMemcpyAsync(&stat, d->status, 4, cudaMemcpyDeviceToHost, d->stream));
   DCUDA(d, cudaStreamSynchronize(d->stream));
   if (stat) return dfail(d, VTQ_ERR_TIMEOUT, "decode: a device-side wait timed out");
+  return VTQ_OK;
+}
+
+// Diagnostic: copy one of the session's activation buffers (as left by the
+// last step) to host memory. 0 x, 1 xb, 2 q, 3 k, 4 v, 5 xo, 6 xb2, 7 g,
+// 8 u, 9 inner, 10 logits; n is the element count to copy.
+vtq_status vtq_decode_debug_buffer(vtq_decode* d, int which, float* out, size_t n) {
+  if (!d || !out) return VTQ_ERR_INVALID_ARG;
+  float* bufs[] = {d->x, d->xb, d->q, d->k, d->v, d->xo, d->xb2, d->g, d->u, d->inner, d->logits};
+  if (which < 0 || which > 10) return VTQ_ERR_INVALID_ARG;
+  DCUDA(d, cudaMemcpyAsync(out, bufs[which], n * 4, cudaMemcpyDeviceToHost, d->stream));
+  DCUDA(d, cudaStreamSynchronize(d->stream));
   return VTQ_OK;
 }
 

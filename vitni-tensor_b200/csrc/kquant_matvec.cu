@@ -577,7 +577,9 @@ cudaError_t launch_kq_matvec(const DevMatrix& m, const float* x, int64_t ldx, in
     p.status = status;
     p.lpr = lpr;
     const int NB = m.dtype == T_Q4_K ? BsumStride<8>::v : BsumStride<16>::v;
-    uint32_t off = 256;  // mbarriers
+    constexpr uint32_t kBarBytes = (2 * KQ_NST_MAX + 1) * 8;  // full[], empty[], xbar
+    static_assert(kBarBytes <= 512, "barrier area");
+    uint32_t off = 512;  // mbarriers (kBarBytes) live below this offset
     p.off_xd = off;
     off = align_up(off + nb * S * 4, 16);
     p.off_bsum = off;
