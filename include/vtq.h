@@ -128,6 +128,21 @@ vtq_status vtq_linear_device(int32_t dtype, const uint8_t* w_dev, int64_t in_fea
                              int64_t batch, uint32_t flags, uint32_t* status_dev,
                              void* cuda_stream);
 
+/* Q4_K / Q6_K integer linear with host x and y that allocates nothing: for
+ * callers that cannot call cudaMalloc (their device memory is owned by a pool
+ * or budget they do not control, or allocation is not allowed on their path).
+ * No counterpart in the reference. Same arithmetic and result as vtq_linear
+ * with VTQ_PTR_HOST; w_dev is caller-owned device memory in the layout of
+ * vtq_device_repack. x, y and the status word are staged in one static device
+ * array of 1 MiB (256K floats, kept by every GPU that loads the library until
+ * exit): 64 + batch*in_feat + batch*rows floats must fit, else VTQ_ERR_INTERNAL.
+ * All calls on a device share that array, so calls that overlap on the GPU
+ * race. The first call on a device looks the array's address up; make it
+ * before any stream capture. Synchronous: returns when y is written. */
+vtq_status vtq_linear_host_noalloc(int32_t dtype, const uint8_t* w_dev, int64_t in_feat,
+                                   int64_t rows, const float* x, float* y, int64_t batch,
+                                   void* cuda_stream);
+
 /* ---- Quantized decode session: a GGUF Llama model resident on
  * one device; the decode step of src/model/forward_quantized.rs:329-649 and the
  * prompt + greedy loop of src/model/inference.rs:312-327 run as one CUDA graph

@@ -37,7 +37,7 @@ EXPORTS = (
     "vtq_linear_q4_k_fused", "vtq_linear_q4_0", "vtq_device_layout_bytes",
     "vtq_device_repack", "vtq_linear_device", "vtq_decode_open", "vtq_decode_last_error",
     "vtq_decode_config", "vtq_decode_run", "vtq_decode_close", "vtq_expf", "vtq_sinf",
-    "vtq_cosf", "vtq_powf", "vtq_libm_sweep",
+    "vtq_cosf", "vtq_powf", "vtq_libm_sweep", "vtq_linear_host_noalloc",
 )
 
 
@@ -126,6 +126,7 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         "vtq_cosf": (ctypes.c_float, [ctypes.c_float]),
         "vtq_powf": (ctypes.c_float, [ctypes.c_float, ctypes.c_float]),
         "vtq_libm_sweep": (None, [c_p, c_sz, c_p]),
+        "vtq_linear_host_noalloc": (c_i32, [c_i32, c_p, c_i64, c_i64, c_p, c_p, c_i64, c_p]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
