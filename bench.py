@@ -201,6 +201,99 @@ def cpu_baseline(cfg_name, budget_s=12.0):
                       "(oracle restatement of the reference's row-parallel integer linears)"}
 
 
+DECODE_CFG = "c4_tinyllama_decode"
+
+
+def decode_bytes_per_token(cfg, n_pos):
+    """Algorithmic HBM bytes of one decode step averaged over positions 0..n_pos-1:
+    every weight once (packed) + norms + the embedding row + KV reads 2*kv_dim*4*(pos+1)
+    per layer."""
+    from vtq import formats
+    d, h, L, V = cfg["dim"], cfg["hidden"], cfg["layers"], cfg["vocab"]
+    kv = cfg["kv_heads"] * (d // cfg["heads"])
+    q4, q6 = formats.Q4_K, formats.Q6_K
+    w = L * (formats.row_bytes(q4, d) * (2 * d + kv + 2 * h) + formats.row_bytes(q6, d) * kv +
+             formats.row_bytes(q6, h) * d)
+    w += formats.row_bytes(q6, d) * V + formats.row_bytes(q4, d) + 4 * d * (2 * L + 1)
+    kv_avg = L * 2 * kv * 4 * (n_pos + 1) / 2
+    return w + kv_avg
+
+
+def run_decode(args, world, rank, local):
+    """TinyLlama-shaped Q4_K/Q6_K model, 16 prompt + 64 greedy
+    tokens per step of the benchmark; replicas on N GPUs (decode does not shard)."""
+    import torch
+    import torch.distributed as dist
+    import vtq
+    from vtq import gguf, receipt
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    cfg = gguf.TINYLLAMA
+    blob = gguf.synthetic_llama(cfg)
+    prompt = gguf.prompt_tokens(16, cfg["vocab"])
+    n_new = 64
+    sess = vtq.DecodeSession(blob, local)
+    for _ in range(max(1, args.warmup // 10)):
+        toks, _ = sess.run(prompt, n_new)
+    reps = max(1, min(args.steps, 20))
+    clocks = ClockSampler(local)
+    if world > 1:
+        dist.barrier()
+    clocks.start()
+    steps_ms, call_ms = 0.0, 0.0
+    for _ in range(reps):
+        toks2, _ = sess.run(prompt, n_new)
+        a, b = sess.timing()
+        steps_ms += a
+        call_ms += b
+    clk = clocks.stop()
+    assert toks2 == toks
+    if world > 1:
+        t = torch.tensor([steps_ms, call_ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        steps_ms, call_ms = float(t[0]), float(t[1])
+    n_pos = len(prompt) + n_new
+    tok_s = reps * n_pos * world / (steps_ms / 1e3)
+    e2e = reps * n_pos * world / (call_ms / 1e3)
+    per_tok_bytes = decode_bytes_per_token(cfg, n_pos)
+    peak, peak_kind = peaks()
+    achieved = per_tok_bytes / (steps_ms / reps / n_pos / 1e3) / 1e9
+    rc = receipt.decode_receipt(gguf.MODEL_ID, blob, gguf.arch_string(cfg), prompt, n_new, toks)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        from oracle import oracle as O
+        threads = os.cpu_count() or 1
+        t0 = time.perf_counter()
+        ref, _ = O.decode_run(blob, prompt, n_new, threads=threads)
+        el = time.perf_counter() - t0
+        cpu = {"value": round(n_pos / el, 3), "unit": "tok/s", "cores": threads, "kind": "port",
+               "sample": f"one full config-4 run ({n_pos} positions) in {el:.1f} s",
+               "tokens_match": ref == toks}
+    if rank == 0:
+        print(json.dumps({
+            "metric": METRIC, "value": round(tok_s, 2), "unit": "tok/s", "n_gpus": world,
+            "steps": reps, "warmup": max(1, args.warmup // 10),
+            "ms_per_step": round(steps_ms / reps, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "config": {"workload": DECODE_CFG, "model": "random-init TinyLlama-1.1B shapes, "
+                       "Q4_K/Q6_K GGUF", "prompt": len(prompt), "new_tokens": n_new,
+                       "parallelism": f"replicas x{world}" if world > 1 else "1 GPU",
+                       "l2": "667 MB of weights per token > L2",
+                       "timing": "CUDA events around the graph launches of one run"},
+            "ms_per_token": round(steps_ms / reps / n_pos, 4),
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                         "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": None,
+                         "peak_source": peak_kind, "bytes_per_token": per_tok_bytes},
+            "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": 4 * len(prompt),
+                    "d2h_bytes_per_step": 4 * n_new + 4},
+            "receipt": {"model_digest": rc["model_digest"], "model_digest_v1": rc["model_digest_v1"]},
+            "gpu_launches": None, "clocks": clk, "cpu_baseline": cpu}), flush=True)
+    sess.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -219,6 +312,9 @@ def main():
 
     if args.impl == "reference":
         run_reference(args, world, rank)
+        return
+    if args.config == DECODE_CFG:
+        run_decode(args, world, rank, local)
         return
 
     import torch

@@ -160,6 +160,13 @@ vtq_status vtq_decode_config(const vtq_decode* d, int64_t* out8);
  * n_new generated ids; logits (optional) receives (n_prompt + n_new) x vocab. */
 vtq_status vtq_decode_run(vtq_decode* d, const uint32_t* prompt, size_t n_prompt, size_t n_new,
                           uint32_t* out_tokens, float* logits);
+/* Device time of the last vtq_decode_run, CUDA events on the session stream:
+ * ms2[0] = the decode steps alone, ms2[1] = the whole call including the prompt
+ * upload and the token / logits read-back. No reference counterpart. */
+vtq_status vtq_decode_timing(const vtq_decode* d, float* ms2);
+/* Diagnostic: copy an activation buffer left by the last step (0 x, 1 xb, 2 q,
+ * 3 k, 4 v, 5 xo, 6 xb2, 7 gate, 8 up, 9 SwiGLU, 10 logits); n elements. */
+vtq_status vtq_decode_debug_buffer(vtq_decode* d, int which, float* out, size_t n);
 vtq_status vtq_decode_close(vtq_decode* d);
 
 /* ---- Software transcendentals shared by host and device. ----

@@ -443,6 +443,8 @@ struct vtq_decode {
   unsigned* status = nullptr;
   cudaGraphExec_t graph = nullptr;
   bool graph_logs = false;
+  cudaEvent_t ev[4] = {};  // call start, first step, after last step, call end
+  float ms_steps = 0.0f, ms_call = 0.0f;
   std::string err;
 };
 
@@ -754,10 +756,15 @@ vtq_status vtq_decode_run(vtq_decode* d, const uint32_t* prompt, size_t n_prompt
     cudaGraphDestroy(graph);
     d->graph_logs = want_logits;
   }
+  if (!d->ev[0])
+    for (auto& e : d->ev) DCUDA(d, cudaEventCreate(&e));
+  DCUDA(d, cudaEventRecord(d->ev[0], d->stream));
   StepState hs{0, prompt[0], (int)n_prompt, (int)total, 0};
   DCUDA(d, cudaMemcpyAsync(d->st, &hs, sizeof hs, cudaMemcpyHostToDevice, d->stream));
   DCUDA(d, cudaMemcpyAsync(d->prompt, prompt, n_prompt * 4, cudaMemcpyHostToDevice, d->stream));
+  DCUDA(d, cudaEventRecord(d->ev[1], d->stream));
   for (size_t pos = 0; pos < total; pos++) DCUDA(d, cudaGraphLaunch(d->graph, d->stream));
+  DCUDA(d, cudaEventRecord(d->ev[2], d->stream));
   if (n_new)
     DCUDA(d, cudaMemcpyAsync(out_tokens, d->out_tokens, n_new * 4, cudaMemcpyDeviceToHost,
                              d->stream));
@@ -766,8 +773,18 @@ vtq_status vtq_decode_run(vtq_decode* d, const uint32_t* prompt, size_t n_prompt
                              d->stream));
   unsigned stat = 0;
   DCUDA(d, cudaMemcpyAsync(&stat, d->status, 4, cudaMemcpyDeviceToHost, d->stream));
+  DCUDA(d, cudaEventRecord(d->ev[3], d->stream));
   DCUDA(d, cudaStreamSynchronize(d->stream));
+  DCUDA(d, cudaEventElapsedTime(&d->ms_steps, d->ev[1], d->ev[2]));
+  DCUDA(d, cudaEventElapsedTime(&d->ms_call, d->ev[0], d->ev[3]));
   if (stat) return dfail(d, VTQ_ERR_TIMEOUT, "decode: a device-side wait timed out");
+  return VTQ_OK;
+}
+
+vtq_status vtq_decode_timing(const vtq_decode* d, float* ms2) {
+  if (!d || !ms2) return VTQ_ERR_INVALID_ARG;
+  ms2[0] = d->ms_steps;
+  ms2[1] = d->ms_call;
   return VTQ_OK;
 }
 
@@ -788,6 +805,8 @@ vtq_status vtq_decode_close(vtq_decode* d) {
   cudaSetDevice(d->device);
   if (d->stream) cudaStreamSynchronize(d->stream);
   if (d->graph) cudaGraphExecDestroy(d->graph);
+  for (auto e : d->ev)
+    if (e) cudaEventDestroy(e);
   for (void* p : d->allocs) cudaFree(p);
   if (d->stream) cudaStreamDestroy(d->stream);
   delete d;

@@ -38,6 +38,7 @@ EXPORTS = (
     "vtq_device_repack", "vtq_linear_device", "vtq_decode_open", "vtq_decode_last_error",
     "vtq_decode_config", "vtq_decode_run", "vtq_decode_close", "vtq_expf", "vtq_sinf",
     "vtq_cosf", "vtq_powf", "vtq_libm_sweep", "vtq_linear_host_noalloc",
+    "vtq_decode_timing", "vtq_decode_debug_buffer",
 )
 
 
@@ -126,6 +127,8 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         "vtq_cosf": (ctypes.c_float, [ctypes.c_float]),
         "vtq_powf": (ctypes.c_float, [ctypes.c_float, ctypes.c_float]),
         "vtq_libm_sweep": (None, [c_p, c_sz, c_p]),
+        "vtq_decode_timing": (c_i32, [c_p, c_p]),
+        "vtq_decode_debug_buffer": (c_i32, [c_p, ctypes.c_int, c_p, c_sz]),
         "vtq_linear_host_noalloc": (c_i32, [c_i32, c_p, c_i64, c_i64, c_p, c_p, c_i64, c_p]),
     }
     for name, (res, args) in sig.items():
@@ -304,6 +307,12 @@ class DecodeSession:
         if st != OK:
             raise _ERRORS.get(st, Error)(self.lib.vtq_decode_last_error(self.handle).decode())
         return out[:n_new].tolist(), lg
+
+    def timing(self):
+        """(ms of the decode steps, ms of the whole last run call), device time."""
+        t = np.zeros(2, np.float32)
+        self.lib.vtq_decode_timing(self.handle, _ptr(t))
+        return float(t[0]), float(t[1])
 
     def close(self):
         if getattr(self, "handle", None):
