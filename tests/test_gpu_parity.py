@@ -47,6 +47,9 @@ SMALL = [  # (dtype, in_feat, out_feat, batch)
     (vtq.Q4_K, 14336, 150, 2), (vtq.Q4_K, 2048, 300, 9), (vtq.Q4_K, 4096, 1, 3),
     (vtq.Q6_K, 256, 1, 1), (vtq.Q6_K, 768, 13, 1), (vtq.Q6_K, 5632, 41, 1),
     (vtq.Q6_K, 14336, 150, 2), (vtq.Q6_K, 2048, 300, 9), (vtq.Q6_K, 4352, 3, 1),
+    # Long rows and many rows per CTA: the ring holds fewer stages than there
+    # are consumer warps, so warps start several ring laps apart.
+    (vtq.Q4_K, 32768, 2000, 1), (vtq.Q6_K, 32768, 1200, 2), (vtq.Q4_K, 24576, 1500, 5),
     (vtq.Q8_0, 32, 1, 1), (vtq.Q8_0, 96, 17, 1), (vtq.Q8_0, 8224, 19, 2),
     (vtq.Q8_0, 4096, 33, 5), (vtq.Q8_0, 16416, 5, 1),
     (vtq.Q5_0, 32, 3, 1), (vtq.Q5_0, 1504, 21, 1), (vtq.Q5_0, 9216, 9, 1),

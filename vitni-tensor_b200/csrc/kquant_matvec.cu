@@ -44,8 +44,15 @@ template <int NB> struct BsumStride { static constexpr int v = NB + 4; };
 constexpr uint32_t FULL = 0xffffffffu;
 
 #ifdef VTQ_TRACE
-__device__ unsigned long long g_kq_trace[1024][8];
-#define KQ_TRACE(slot) g_kq_trace[blockIdx.x][slot] = (slot == 0 ? globaltimer() : clock64())
+// Diagnostic build only: per-CTA %globaltimer stamps for up to 8 launches,
+// selected by their output pointer (set by a host-side probe).
+__device__ unsigned long long g_kq_trace[8][1024][8];
+__device__ const float* g_kq_trace_y[8];
+#define KQ_TRACE(slot)                                                      \
+  do {                                                                      \
+    for (int ti_ = 0; ti_ < 8; ti_++)                                       \
+      if (g_kq_trace_y[ti_] == p.y) g_kq_trace[ti_][blockIdx.x][slot] = globaltimer(); \
+  } while (0)
 #else
 #define KQ_TRACE(slot) (void)0
 #endif
@@ -356,8 +363,17 @@ __device__ __forceinline__ void grid_dep_launch() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
+#ifndef VTQ_KQ_CTAS
+#define VTQ_KQ_CTAS 1
+#endif
+#ifndef VTQ_KQ_XMAX
+#define VTQ_KQ_XMAX 65536
+#endif
+#ifndef VTQ_KQ_CW1
+#define VTQ_KQ_CW1 16
+#endif
 template <int QT, int MAXB, int NCH, int CW>
-__global__ void __launch_bounds__((CW + 1) * 32, 1) kq_matvec_kernel(const KqParams p) {
+__global__ void __launch_bounds__((CW + 1) * 32, VTQ_KQ_CTAS) kq_matvec_kernel(const KqParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
   uint64_t* empty = full + KQ_NST_MAX;
@@ -453,11 +469,16 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1) kq_matvec_kernel(const KqPar
   for (int k = 0; k < nstages; k++) {
     const int buf = k % p.nst;
     const int gend = min((k + 1) * gps, (nrows + rpw - 1) / rpw);
+    // Every warp waits for every stage in order, also for stages where it
+    // has no rows: a parity wait is only unambiguous one phase ahead, so a
+    // warp that first waited on stage k + nst (same buffer, other parity)
+    // would pass on the barrier's initial state. The in-order waits also
+    // keep the CTA alive until all of its bulk copies have landed.
+    if (!mbar_wait_bounded(&full[buf], (uint32_t)((k / p.nst) & 1))) {
+      if (lane == 0) record_error(p.status, KERR_TIMEOUT);
+      return;
+    }
     if (g < gend) {
-      if (!mbar_wait_bounded(&full[buf], (uint32_t)((k / p.nst) & 1))) {
-        if (lane == 0) record_error(p.status, KERR_TIMEOUT);
-        return;
-      }
       if (tid == 0 && k == 0) KQ_TRACE(3);
       const uint8_t* sbuf = stg + (size_t)buf * p.stage_bytes;
       for (; g < gend; g += CW) {
@@ -509,7 +530,7 @@ cudaError_t launch_variant(const KqParams& p, int grid, uint32_t smem, cudaStrea
 template <int QT, int MAXB>
 cudaError_t launch_nch(const KqParams& p, int grid, uint32_t smem, cudaStream_t st) {
   const int nch = (p.S + 31) / 32;
-  constexpr int CW = MAXB <= 2 ? 16 : 8;
+  constexpr int CW = MAXB <= 1 ? VTQ_KQ_CW1 : (MAXB <= 2 ? 16 : 8);
   if (nch <= 1) return launch_variant<QT, MAXB, 1, CW>(p, grid, smem, st);
   if (nch == 2) return launch_variant<QT, MAXB, 2, CW>(p, grid, smem, st);
   return launch_variant<QT, MAXB, 4, CW>(p, grid, smem, st);
@@ -553,7 +574,14 @@ cudaError_t launch_kq_matvec(const DevMatrix& m, const float* x, int64_t ldx, in
   const int S = (int)(m.in_feat / 256);
   if (S < 1 || S > KQ_SMAX || m.in_feat % 256) return cudaErrorInvalidValue;
   if (m.out_feat <= 0 || batch <= 0) return cudaSuccess;
-  const int smem_max = max_smem_optin();
+  int smem_max = max_smem_optin();
+  if (VTQ_KQ_CTAS == 2) {
+    int dev = 0, per_sm = 0, resv = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
+    cudaDeviceGetAttribute(&resv, cudaDevAttrReservedSharedMemoryPerBlock, dev);
+    smem_max = std::min(smem_max, per_sm / 2 - resv);
+  }
   const int nsm = num_sms();
   int lpr = 1;
   while (lpr < S && lpr < 32) lpr <<= 1;
@@ -589,7 +617,7 @@ cudaError_t launch_kq_matvec(const DevMatrix& m, const float* x, int64_t ldx, in
     // Stage x through TMA when every row start is 16-byte aligned and it fits.
     const uint32_t xbytes = (uint32_t)(nb * p.n * 4);
     p.x_smem = ((reinterpret_cast<uintptr_t>(p.x) & 15u) == 0 && (ldx % 4) == 0 &&
-                xbytes <= 65536u) ? 1 : 0;
+                xbytes <= (uint32_t)VTQ_KQ_XMAX) ? 1 : 0;
     p.off_xf = off;
     if (p.x_smem) off = align_up(off + xbytes, 128);
     p.off_stage = off;
