@@ -1,0 +1,544 @@
+// kquant_gemm.cu -- batched (prefill-sized) exact-integer Q4_K linear on the
+// sm_100a tensor cores (tcgen05.mma kind::i8, int32 accumulators in TMEM).
+//
+// Computes, bit for bit, vitni-tensor's integer Q4_K linear for many
+// activation rows at once:
+//   linear_q4_k_integer(_parallel)  src/ops/quant.rs:936-980, :1149-1196
+// y[b, o] = fixed_tree_s( (d_os * xd_bs) * f32(acc) - (dmin_os * xd_bs) * f32(acc_m) )
+//   acc   = sum_j sc_j * sum_l q_jl * xq_bjl      (dot_q4k_q8_block, quant.rs:850-898)
+//   acc_m = sum_j mn_j * bsum_bj
+// Each activation row is quantised per 256-block exactly like
+// quantize_block_q8 (quant.rs:750-771), independently of the other rows.
+//
+// Tensor-core mapping. For one superblock s both integers are contractions
+// over its 256 positions k, so they are computed as one MMA product of the
+// activation tile (A: 128 tokens x 256 int8, K-major) with three unsigned
+// byte planes of the weights (B: 96 "rows" x 256):
+//   rows  0..31  lo_k = (sc_j(k) * q_k) & 127
+//   rows 32..63  hi_k = (sc_j(k) * q_k) >> 7          (sc * q <= 945 < 1024)
+//   rows 64..95  mn_j(k)                              (the 6-bit min, repeated)
+// so acc = D[:, r] + 128 * D[:, 32 + r] and acc_m = D[:, 64 + r] exactly
+// (|acc| <= 256 * 127 * 945 < 2^31). The planes are built in shared memory
+// from the packed superblocks by two builder warps; the per-superblock fp
+// combine and the cross-superblock fixed_tree stay on CUDA cores, in the
+// reference's op order, with the tree kept per (token, row) in registers as a
+// binary counter of complete subtrees (identical pairings to the level-wise
+// loop of quant.rs:462-476).
+//
+// CTA = 128 tokens x 32 weight rows, looping over superblocks:
+//   warp 0      TMA producer: activation tile (2 x 16 KB, 128B-swizzled) and
+//               the 32 rows' superblock (32 x 144 B) per step
+//   warp 1      TMEM owner; lane 0 issues 8 MMAs (K = 32 each) per step
+//   warps 2-3   plane builders (64 threads: one row x one 128-position half)
+//   warps 4-11  epilogue: TMEM -> registers, fp combine, fixed_tree
+// Every wait is bounded (%globaltimer); a timeout sets the status word, stops
+// the pipeline and still frees TMEM.
+#include <cuda.h>
+#include <cuda_fp16.h>
+
+#include <mutex>
+#include <unordered_map>
+
+#include "vtq_device.cuh"
+#include "vtq_internal.h"
+
+namespace vtq {
+namespace {
+
+constexpr int GM = 128;         // tokens per CTA = MMA M = TMEM lanes
+constexpr int GR = 32;          // weight rows per CTA
+constexpr int GN = 3 * GR;      // MMA N: lo | hi | mins
+constexpr int NX = 3;           // activation stages
+constexpr int NW = 4;           // packed-weight stages
+constexpr int NP = 2;           // plane stages
+constexpr int NMETA = 4;        // d / dmin stages
+constexpr uint32_t X_STAGE = GM * 256;  // 2 K-blocks x 16 KB
+constexpr uint32_t P_STAGE = GN * 256;  // 2 K-blocks x 12 KB
+constexpr uint32_t P_KBLK = GN * 128;
+constexpr uint32_t W_STAGE = GR * 144;
+constexpr uint32_t TMEM_COLS = 256;     // two accumulator buffers of GN columns
+constexpr int kBuildWarps = 2, kEpiWarps = 8;
+constexpr int kThreads = 32 * (2 + kBuildWarps + kEpiWarps);
+
+// Shared-memory map (offsets from a 1024-aligned base).
+constexpr uint32_t OFF_X = 0;
+constexpr uint32_t OFF_P = OFF_X + NX * X_STAGE;
+constexpr uint32_t OFF_W = OFF_P + NP * P_STAGE;
+constexpr uint32_t OFF_META = OFF_W + NW * W_STAGE;
+constexpr uint32_t OFF_BAR = OFF_META + NMETA * GR * 8;
+constexpr int NBAR = 2 * (NX + NW + NP + NMETA + 2);
+constexpr uint32_t OFF_SLOT = OFF_BAR + NBAR * 8;
+constexpr uint32_t SMEM_BYTES = OFF_SLOT + 16 + 1024;  // + alignment slack
+
+struct GemmParams {
+  int M, n, S, R;
+  float* y;
+  int64_t ldy;
+  const float* xd;  // [M][S] activation block scales
+  unsigned* status;
+};
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* tm, int x, int y,
+                                            uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, "
+      "{%2, %3}], [%4];" ::"r"(dst),
+      "l"(tm), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+
+// UMMA shared-memory descriptor, K-major, 128-byte swizzle: 8-row groups
+// 1024 B apart (SBO), version 1, layout type 2.
+__device__ __forceinline__ uint64_t desc_sw128(uint32_t saddr) {
+  uint64_t d = (uint64_t)((saddr >> 4) & 0x3fffu);
+  d |= (uint64_t)1 << 16;               // LBO (unused for swizzled K-major)
+  d |= (uint64_t)(1024 >> 4) << 32;     // SBO
+  d |= (uint64_t)1 << 46;               // descriptor version
+  d |= (uint64_t)2 << 61;               // SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor: D s32, A s8 (activations), B u8 (planes), both
+// K-major, N = GN, M = GM.
+constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (0u << 10) | ((uint32_t)(GN >> 3) << 17) |
+                            ((uint32_t)(GM >> 4) << 24);
+
+__device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(a), "l"(b), "r"(kIdesc), "r"(acc), "r"(0), "r"(0), "r"(0), "r"(0));
+}
+
+__device__ __forceinline__ void mma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+               : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, int (&r)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+                 "=r"(r[7])
+               : "r"(taddr));
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ bool wait_u32(uint32_t bar, uint32_t parity) {
+  return mbar_wait_bounded(reinterpret_cast<uint64_t*>(__cvta_shared_to_generic(bar)), parity);
+}
+
+// Byte offset of (plane row nr, position k in [0, 256)) in a plane stage:
+// two K-blocks of 128 positions, 8-row atoms of 1024 B, 16-byte chunks
+// XOR-swizzled by the row within the atom (the TMA/UMMA 128B pattern).
+__device__ __forceinline__ uint32_t plane_off(int nr, int k) {
+  const int kb = k >> 7, chunk = (k & 127) >> 4;
+  return (uint32_t)(kb * P_KBLK + (nr >> 3) * 1024 + (nr & 7) * 128 + ((chunk ^ (nr & 7)) << 4));
+}
+
+// sc * q for the four nibble bytes of `nib`, split into (low 7 bits, high bits).
+__device__ __forceinline__ void scale_split(uint32_t nib, uint32_t sc, uint32_t& lo, uint32_t& hi) {
+  const uint32_t pe = (nib & 0x00FF00FFu) * sc;          // bytes 0 and 2 in 16-bit lanes
+  const uint32_t po = ((nib >> 8) & 0x00FF00FFu) * sc;   // bytes 1 and 3
+  lo = (pe & 0x007F007Fu) | ((po & 0x007F007Fu) << 8);
+  hi = ((pe >> 7) & 0x00070007u) | (((po >> 7) & 0x00070007u) << 8);
+}
+
+__device__ __forceinline__ float h2f(uint32_t bits) {
+  return __half2float(__ushort_as_half((unsigned short)bits));
+}
+
+template <int LV>
+__global__ void __launch_bounds__(kThreads, 1)
+    kq_gemm_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmw,
+                   const GemmParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;
+  uint8_t* gbase = smem_raw + (base - smem_u32(smem_raw));
+  const uint32_t bar0 = base + OFF_BAR;
+  auto X_FULL = [&](int i) { return bar0 + 8u * i; };
+  auto X_EMPTY = [&](int i) { return bar0 + 8u * (NX + i); };
+  auto W_FULL = [&](int i) { return bar0 + 8u * (2 * NX + i); };
+  auto W_EMPTY = [&](int i) { return bar0 + 8u * (2 * NX + NW + i); };
+  auto P_FULL = [&](int i) { return bar0 + 8u * (2 * NX + 2 * NW + i); };
+  auto P_EMPTY = [&](int i) { return bar0 + 8u * (2 * NX + 2 * NW + NP + i); };
+  auto M_FULL = [&](int i) { return bar0 + 8u * (2 * NX + 2 * NW + 2 * NP + i); };
+  auto M_EMPTY = [&](int i) { return bar0 + 8u * (2 * NX + 2 * NW + 2 * NP + NMETA + i); };
+  auto A_FULL = [&](int i) { return bar0 + 8u * (2 * NX + 2 * NW + 2 * NP + 2 * NMETA + i); };
+  auto A_EMPTY = [&](int i) { return bar0 + 8u * (2 * NX + 2 * NW + 2 * NP + 2 * NMETA + 2 + i); };
+  volatile uint32_t* slot = reinterpret_cast<volatile uint32_t*>(gbase + OFF_SLOT);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(gbase + OFF_SLOT + 4);
+  float2* meta = reinterpret_cast<float2*>(gbase + OFF_META);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int tok0 = blockIdx.x * GM, row0 = blockIdx.y * GR;
+  const int S = p.S;
+
+  if (tid == 0) {
+    auto init = [](uint32_t b, unsigned c) {
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(b), "r"(c));
+    };
+    for (int i = 0; i < NX; i++) { init(X_FULL(i), 1); init(X_EMPTY(i), 1); }
+    for (int i = 0; i < NW; i++) { init(W_FULL(i), 1); init(W_EMPTY(i), 32 * kBuildWarps); }
+    for (int i = 0; i < NP; i++) { init(P_FULL(i), 32 * kBuildWarps); init(P_EMPTY(i), 1); }
+    for (int i = 0; i < NMETA; i++) { init(M_FULL(i), 32 * kBuildWarps); init(M_EMPTY(i), kEpiWarps); }
+    for (int i = 0; i < 2; i++) { init(A_FULL(i), 1); init(A_EMPTY(i), kEpiWarps); }
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(base + OFF_SLOT),
+                 "r"(TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *slot;
+
+  auto fail = [&]() {
+    record_error(p.status, KERR_TIMEOUT);
+    *abort_flag = 1;
+  };
+
+  if (warp == 0) {
+    // ---- producer ----
+    if (lane == 0) {
+      for (int s = 0; s < S && !*abort_flag; s++) {
+        const int sx = s % NX, sw = s % NW;
+        if (!wait_u32(X_EMPTY(sx), ((s / NX) + 1) & 1)) { fail(); break; }
+        mbar_arrive_expect_tx(reinterpret_cast<uint64_t*>(gbase + OFF_BAR + 8 * sx), X_STAGE);
+        const uint32_t xs = base + OFF_X + sx * X_STAGE;
+        tma_load_2d(xs, &tmx, 256 * s, tok0, X_FULL(sx));
+        tma_load_2d(xs + X_STAGE / 2, &tmx, 256 * s + 128, tok0, X_FULL(sx));
+        if (!wait_u32(W_EMPTY(sw), ((s / NW) + 1) & 1)) { fail(); break; }
+        mbar_arrive_expect_tx(reinterpret_cast<uint64_t*>(gbase + OFF_BAR + 8 * (2 * NX + sw)),
+                              W_STAGE);
+        tma_load_2d(base + OFF_W + sw * W_STAGE, &tmw, 144 * s, row0, W_FULL(sw));
+      }
+    }
+  } else if (warp == 1) {
+    // ---- MMA issuer ----
+    if (lane == 0) {
+      for (int s = 0; s < S && !*abort_flag; s++) {
+        const int sx = s % NX, sp = s % NP, ab = s & 1;
+        if (!wait_u32(X_FULL(sx), (s / NX) & 1) || !wait_u32(P_FULL(sp), (s / NP) & 1) ||
+            !wait_u32(A_EMPTY(ab), ((s >> 1) + 1) & 1)) {
+          fail();
+          break;
+        }
+        tc_fence_after();
+        const uint32_t xs = base + OFF_X + sx * X_STAGE, ps = base + OFF_P + sp * P_STAGE;
+        const uint32_t d = tmem + (uint32_t)ab * 128u;
+#pragma unroll
+        for (int c = 0; c < 8; c++) {
+          const uint32_t kb = (uint32_t)(c >> 2), ko = (uint32_t)(c & 3) * 32u;
+          mma_i8(d, desc_sw128(xs + kb * (X_STAGE / 2) + ko), desc_sw128(ps + kb * P_KBLK + ko),
+                 c > 0 ? 1u : 0u);
+        }
+        mma_commit(X_EMPTY(sx));
+        mma_commit(P_EMPTY(sp));
+        mma_commit(A_FULL(ab));
+      }
+    }
+  } else if (warp < 2 + kBuildWarps) {
+    // ---- plane builders: thread = (row r, K-block kb) ----
+    const int t = tid - 64, r = t >> 1, kb = t & 1;
+    for (int s = 0; s < S && !*abort_flag; s++) {
+      const int sw = s % NW, sp = s % NP, sm = s % NMETA;
+      if (!wait_u32(W_FULL(sw), (s / NW) & 1) || !wait_u32(P_EMPTY(sp), ((s / NP) + 1) & 1) ||
+          !wait_u32(M_EMPTY(sm), ((s / NMETA) + 1) & 1)) {
+        fail();
+        break;
+      }
+      const uint8_t* sb = gbase + OFF_W + sw * W_STAGE + r * 144;
+      const uint4 hdr = *reinterpret_cast<const uint4*>(sb);
+      uint8_t* pl = gbase + OFF_P + sp * P_STAGE;
+      if (kb == 0) meta[sm * GR + r] = make_float2(h2f(hdr.x & 0xffffu), h2f(hdr.x >> 16));
+#pragma unroll
+      for (int jj = 0; jj < 4; jj++) {
+        const int j = 4 * kb + jj;  // sub-block
+        // get_scale_min_k4 (quant.rs:268-276)
+        uint32_t sc, mn;
+        if (j < 4) {
+          sc = (hdr.y >> (8 * j)) & 63;
+          mn = (hdr.z >> (8 * j)) & 63;
+        } else {
+          const int k4 = j - 4;
+          const uint32_t lo4 = (hdr.w >> (8 * k4)) & 0xff;
+          sc = (lo4 & 15) | (((hdr.y >> (8 * k4 + 6)) & 3) << 4);
+          mn = (lo4 >> 4) | (((hdr.z >> (8 * k4 + 6)) & 3) << 4);
+        }
+        const uint32_t mrep = mn * 0x01010101u;
+        const uint8_t* qs = sb + 16 + 32 * (j >> 1);  // pair of sub-blocks sharing bytes
+#pragma unroll
+        for (int h16 = 0; h16 < 2; h16++) {
+          const uint4 w = *reinterpret_cast<const uint4*>(qs + 16 * h16);
+          const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
+          uint32_t lo[4], hi[4];
+#pragma unroll
+          for (int u = 0; u < 4; u++) {
+            const uint32_t nib = (j & 1) ? ((wv[u] >> 4) & 0x0F0F0F0Fu) : (wv[u] & 0x0F0F0F0Fu);
+            scale_split(nib, sc, lo[u], hi[u]);
+          }
+          const int k = 32 * j + 16 * h16;
+          *reinterpret_cast<uint4*>(pl + plane_off(r, k)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+          *reinterpret_cast<uint4*>(pl + plane_off(GR + r, k)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+          *reinterpret_cast<uint4*>(pl + plane_off(2 * GR + r, k)) = make_uint4(mrep, mrep, mrep, mrep);
+        }
+      }
+      // Generic-proxy stores -> visible to the tensor core (async proxy).
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      mbar_arrive(P_FULL(sp));
+      mbar_arrive(M_FULL(sm));
+      mbar_arrive(W_EMPTY(sw));
+    }
+  } else {
+    // ---- epilogue: thread = token (TMEM lane), 16 weight rows ----
+    const int ew = warp - (2 + kBuildWarps);
+    const int q = warp & 3, half = ew >> 2;
+    const int b = tok0 + 32 * q + lane;
+    const bool bvalid = b < p.M;
+    const int rbase = 16 * half;
+    float st[LV][16];
+#pragma unroll
+    for (int L = 0; L < LV; L++)
+#pragma unroll
+      for (int i = 0; i < 16; i++) st[L][i] = 0.0f;
+    float xd_next = bvalid ? p.xd[(int64_t)b * S] : 0.0f;
+    for (int s = 0; s < S && !*abort_flag; s++) {
+      const int ab = s & 1, sm = s % NMETA;
+      const float xdv = xd_next;
+      if (s + 1 < S) xd_next = bvalid ? p.xd[(int64_t)b * S + s + 1] : 0.0f;
+      if (!wait_u32(A_FULL(ab), (s >> 1) & 1) || !wait_u32(M_FULL(sm), (s / NMETA) & 1)) {
+        if (lane == 0) fail();
+        break;
+      }
+      tc_fence_after();
+#pragma unroll
+      for (int hh = 0; hh < 2; hh++) {
+        const int rr = rbase + 8 * hh;
+        const uint32_t ta = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)ab * 128u + (uint32_t)rr;
+        int vlo[8], vhi[8], vmn[8];
+        tmem_ld8(ta, vlo);
+        tmem_ld8(ta + GR, vhi);
+        tmem_ld8(ta + 2 * GR, vmn);
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+          const float2 dm = meta[sm * GR + rr + i];
+          const int acc = vlo[i] + (vhi[i] << 7);
+          const float t0 = __fmul_rn(__fmul_rn(dm.x, xdv), __int2float_rn(acc));
+          const float t1 = __fmul_rn(__fmul_rn(dm.y, xdv), __int2float_rn(vmn[i]));
+          float carry = __fsub_rn(t0, t1);
+          // Binary counter over superblocks: level L holds a complete subtree
+          // of 2^L leaves while bit L of the number of leaves seen is set.
+          bool done = false;
+#pragma unroll
+          for (int L = 0; L < LV; L++) {
+            if (!done) {
+              if ((s >> L) & 1) {
+                carry = __fadd_rn(st[L][8 * hh + i], carry);
+              } else {
+                st[L][8 * hh + i] = carry;
+                done = true;
+              }
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(A_EMPTY(ab));
+        mbar_arrive(M_EMPTY(sm));
+      }
+    }
+    if (!*abort_flag && bvalid) {
+      // Remaining subtrees sit at the set bits of S; fold them right to left.
+#pragma unroll
+      for (int i = 0; i < 16; i++) {
+        float acc = 0.0f;
+        bool have = false;
+#pragma unroll
+        for (int L = 0; L < LV; L++) {
+          if ((S >> L) & 1) {
+            acc = have ? __fadd_rn(st[L][i], acc) : st[L][i];
+            have = true;
+          }
+        }
+        const int o = row0 + rbase + i;
+        if (o < p.R) p.y[(int64_t)b * p.ldy + o] = acc;
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS));
+  }
+}
+
+// quantize_block_q8 (quant.rs:750-771) for every (row, 256-block): one warp
+// per block, 8 contiguous elements per lane; int8 codes to xq [M][n], block
+// scales to xd [M][S].
+__global__ void quantize_rows_kernel(const float* __restrict__ x, int64_t ldx, int M, int n,
+                                     int8_t* __restrict__ xq, float* __restrict__ xd) {
+  const int S = n / 256;
+  const int64_t u = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+  if (u >= (int64_t)M * S) return;
+  const int lane = threadIdx.x & 31;
+  const int b = (int)(u / S), s = (int)(u - (int64_t)b * S);
+  const float* src = x + (int64_t)b * ldx + 256 * s + 8 * lane;
+  float v[8];
+#pragma unroll
+  for (int i = 0; i < 8; i++) v[i] = src[i];
+  uint32_t am = 0;
+#pragma unroll
+  for (int i = 0; i < 8; i++) {
+    const uint32_t bits = __float_as_uint(v[i]) & 0x7fffffffu;
+    if (bits <= 0x7f800000u) am = max(am, bits);
+  }
+  am = __reduce_max_sync(0xffffffffu, am);
+  const float d = __fdiv_rn(__uint_as_float(am), 127.0f);
+  const float inv = (d != 0.0f) ? __fdiv_rn(1.0f, d) : 0.0f;
+  uint32_t w0 = 0, w1 = 0;
+#pragma unroll
+  for (int i = 0; i < 8; i++) {
+    const int qv = q8_round(__fmul_rn(v[i], inv));
+    if (i < 4) w0 |= (uint32_t)(qv & 0xff) << (8 * i);
+    else w1 |= (uint32_t)(qv & 0xff) << (8 * (i - 4));
+  }
+  *reinterpret_cast<uint2*>(xq + (int64_t)b * n + 256 * s + 8 * lane) = make_uint2(w0, w1);
+  if (lane == 0) xd[(int64_t)b * S + s] = d;
+}
+
+typedef CUresult (*EncodeFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                             const cuuint64_t*, const cuuint32_t*, const cuuint32_t*,
+                             CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion,
+                             CUtensorMapFloatOOBfill);
+
+EncodeFn encoder() {
+  static EncodeFn fn = nullptr;
+  static std::mutex mu;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!fn) {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeFn>(f);
+  }
+  return fn;
+}
+
+// 2D byte tensor map [rows][cols] with row stride `pitch`.
+cudaError_t byte_map(CUtensorMap* tm, const void* ptr, int64_t rows, int64_t cols, int64_t pitch,
+                     uint32_t box_x, uint32_t box_y, CUtensorMapSwizzle sw) {
+  EncodeFn enc = encoder();
+  if (!enc) return cudaErrorInvalidValue;
+  cuuint64_t gdim[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t gstride[1] = {(cuuint64_t)pitch};
+  cuuint32_t box[2] = {box_x, box_y};
+  cuuint32_t es[2] = {1, 1};
+  return enc(tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(ptr), gdim, gstride, box, es,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS
+             ? cudaSuccess
+             : cudaErrorInvalidValue;
+}
+
+// Per-device scratch for the quantised activations (grown on demand).
+struct Scratch {
+  uint8_t* ptr = nullptr;
+  size_t cap = 0;
+};
+std::mutex g_scratch_mu;
+Scratch g_scratch[64];
+
+cudaError_t scratch(size_t bytes, uint8_t** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  Scratch& sc = g_scratch[dev];
+  if (sc.cap < bytes) {
+    if (sc.ptr) {
+      cudaError_t e = cudaDeviceSynchronize();
+      if (e != cudaSuccess) return e;
+      cudaFree(sc.ptr);
+      sc.ptr = nullptr;
+      sc.cap = 0;
+    }
+    const size_t cap = (bytes + (1u << 20) - 1) & ~(size_t)((1u << 20) - 1);
+    cudaError_t e = cudaMalloc(&sc.ptr, cap);
+    if (e != cudaSuccess) return e;
+    sc.cap = cap;
+  }
+  *out = sc.ptr;
+  return cudaSuccess;
+}
+
+template <int LV>
+cudaError_t launch_lv(const CUtensorMap& tmx, const CUtensorMap& tmw, const GemmParams& p, dim3 grid,
+                      cudaStream_t st) {
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(kq_gemm_kernel<LV>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)SMEM_BYTES);
+    if (e != cudaSuccess) return e;
+    attr = true;
+  }
+  kq_gemm_kernel<LV><<<grid, kThreads, SMEM_BYTES, st>>>(tmx, tmw, p);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+bool kq_gemm_supported(const DevMatrix& m, int64_t batch) {
+  return m.dtype == T_Q4_K && batch >= 1 && batch <= (int64_t)INT32_MAX / 2 && m.in_feat % 256 == 0 &&
+         m.in_feat / 256 < 128 && m.in_feat >= 256 && m.out_feat <= INT32_MAX &&
+         (int64_t)SMEM_BYTES <= max_smem_optin();
+}
+
+cudaError_t launch_kq_gemm(const DevMatrix& m, const float* x, int64_t ldx, int64_t batch, float* y,
+                           int64_t ldy, unsigned* status, cudaStream_t st) {
+  if (!kq_gemm_supported(m, batch)) return cudaErrorInvalidValue;
+  const int n = (int)m.in_feat, S = n / 256, M = (int)batch, R = (int)m.out_feat;
+  const size_t xq_bytes = ((size_t)M * n + 1023) & ~(size_t)1023;
+  uint8_t* buf = nullptr;
+  cudaError_t e = scratch(xq_bytes + (size_t)M * S * 4, &buf);
+  if (e != cudaSuccess) return e;
+  int8_t* xq = reinterpret_cast<int8_t*>(buf);
+  float* xd = reinterpret_cast<float*>(buf + xq_bytes);
+  {
+    const int64_t blocks = ((int64_t)M * S + 7) / 8;
+    quantize_rows_kernel<<<(unsigned)blocks, 256, 0, st>>>(x, ldx, M, n, xq, xd);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  }
+  CUtensorMap tmx, tmw;
+  if ((e = byte_map(&tmx, xq, M, n, n, 128, GM, CU_TENSOR_MAP_SWIZZLE_128B)) != cudaSuccess) return e;
+  if ((e = byte_map(&tmw, m.data, R, m.pitch, m.pitch, 144, GR, CU_TENSOR_MAP_SWIZZLE_NONE)) !=
+      cudaSuccess)
+    return e;
+  GemmParams p{M, n, S, R, y, ldy, xd, status};
+  const dim3 grid((unsigned)((M + GM - 1) / GM), (unsigned)((R + GR - 1) / GR));
+  // Levels of the fixed-tree counter: floor(log2 S) + 1.
+  int lv = 1;
+  while ((1 << lv) <= S) lv++;
+  if (lv <= 4) return launch_lv<4>(tmx, tmw, p, grid, st);
+  if (lv == 5) return launch_lv<5>(tmx, tmw, p, grid, st);
+  if (lv == 6) return launch_lv<6>(tmx, tmw, p, grid, st);
+  return launch_lv<7>(tmx, tmw, p, grid, st);
+}
+
+}  // namespace vtq

@@ -74,9 +74,20 @@ bool dtype_supported(int dtype) {
          dtype == T_Q4_K || dtype == T_Q6_K;
 }
 
+// From this many activation rows on, integer Q4_K runs on the tensor-core
+// GEMM (one weight pass for all rows) instead of the matvec (one weight pass
+// per 4 rows). Overridable with VTQ_GEMM_MIN_BATCH.
+const int64_t kGemmMinBatch = [] {
+  const char* e = getenv("VTQ_GEMM_MIN_BATCH");
+  return (e && *e) ? (int64_t)atoll(e) : (int64_t)16;
+}();
+
 // Launch the kernel that implements dtype's linear_dispatch arm.
 cudaError_t run_linear(const DevMatrix& m, const float* x, int64_t ldx, float* y, int64_t ldy,
                        int64_t batch, uint32_t flags, unsigned* status, cudaStream_t st) {
+  if (m.dtype == T_Q4_K && !(flags & VTQ_Q4K_FLOAT) && batch >= kGemmMinBatch &&
+      kq_gemm_supported(m, batch))
+    return launch_kq_gemm(m, x, ldx, batch, y, ldy, status, st);
   if (m.dtype == T_Q6_K || (m.dtype == T_Q4_K && !(flags & VTQ_Q4K_FLOAT)))
     return launch_kq_matvec(m, x, ldx, batch, y, ldy, status, st);
   return launch_canon_matvec(m, x, ldx, batch, y, ldy, status, st);

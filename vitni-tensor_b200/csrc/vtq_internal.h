@@ -35,6 +35,12 @@ cudaError_t launch_repack(const uint8_t* staging, const DevMatrix& m, uint8_t* d
 cudaError_t launch_kq_matvec(const DevMatrix& m, const float* x, int64_t ldx, int64_t batch,
                              float* y, int64_t ldy, unsigned* status, cudaStream_t st);
 
+// Batched integer Q4_K linear on the tensor cores (tcgen05 kind::i8): same
+// results as launch_kq_matvec for any batch; used for prefill-sized batches.
+bool kq_gemm_supported(const DevMatrix& m, int64_t batch);
+cudaError_t launch_kq_gemm(const DevMatrix& m, const float* x, int64_t ldx, int64_t batch,
+                           float* y, int64_t ldy, unsigned* status, cudaStream_t st);
+
 // Canonical fp32 matvec (8 pinned lanes, 8192-element chunks, fixed trees)
 // for Q8_0 / Q5_0 / Q4_0 / F32 rows and the float-fused Q4_K mode.
 cudaError_t launch_canon_matvec(const DevMatrix& m, const float* x, int64_t ldx, int64_t batch,
