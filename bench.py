@@ -134,6 +134,21 @@ def run_reference(args, world, rank):
         return
     from vtq import synth
     from oracle import oracle as O
+    if args.config == PREFILL_CFG_NAME:
+        for _ in range(min(args.warmup, 1)):
+            prefill_cpu_sample()
+        samples = [prefill_cpu_sample() for _ in range(max(1, min(args.steps, 3)))]
+        v = statistics.median(x["value"] for x in samples)
+        cpu = dict(samples[0], value=v, sample=f"{len(samples)} steps, each " + samples[0]["sample"])
+        print(json.dumps({
+            "metric": METRIC, "value": v, "unit": "TOPS", "impl": "reference", "n_gpus": world,
+            "steps": len(samples), "warmup": min(args.warmup, 1), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "config": {"workload": args.config, "tokens": synth.PREFILL_M, "l2": "host run"},
+            "cpu_baseline": cpu,
+            "e2e": {"value": v, "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),
+            flush=True)
+        return
     cfg = synth.CONFIGS[args.config]
     mats = [(dt, n, r, synth.weight(dt, f"{args.config}.w.{n}x{r}", r, n),
              synth.activation(f"{args.config}.x.{n}", 1, n)) for dt, n, r in cfg]
@@ -202,6 +217,197 @@ def cpu_baseline(cfg_name, budget_s=12.0):
 
 
 DECODE_CFG = "c4_tinyllama_decode"
+PREFILL_CFG_NAME = "c5_q4_k_prefill_mistral"
+
+
+def int8_peak_tops():
+    """Dense int8 tensor peak measured here with cuBLASLt (torch._int_mm, 8192^3,
+    best of 10 after warm-up); falls back to 2x the measured bf16 peak."""
+    import torch
+    try:
+        n = 8192
+        a = torch.randint(-64, 64, (n, n), dtype=torch.int8, device="cuda")
+        b = torch.randint(-64, 64, (n, n), dtype=torch.int8, device="cuda").t()
+        for _ in range(3):
+            torch._int_mm(a, b)
+        best = None
+        for _ in range(10):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            torch._int_mm(a, b)
+            e1.record()
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1)
+            best = ms if best is None else min(best, ms)
+        del a, b
+        return 2 * n ** 3 / (best / 1e3) / 1e12, "cuBLASLt int8 torch._int_mm 8192^3, measured in this run"
+    except Exception:
+        try:
+            with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+                return 2 * float(json.load(f)["bf16_tflops"]), "2x measured bf16 (MEASURED_PEAKS.json)"
+        except Exception:
+            return 2 * 1590.0, "2x fallback bf16"
+
+
+def prefill_ops(M, linears):
+    return sum(2 * M * n * r for _, n, r in linears)
+
+
+def run_prefill(args, world, rank, local):
+    """the seven Q4_K linears of one Mistral-7B layer at M = 512
+    tokens, batched integer path (tcgen05 kind::i8). A step runs all seven
+    through vtq_linear on device pointers. N > 1: output rows sharded over the
+    ranks (contiguous ranges), y all-gathered over NCCL inside the timed region."""
+    import torch
+    import torch.distributed as dist
+    import vtq
+    from vtq import synth, shard
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    M, lins = synth.PREFILL_M, synth.PREFILL_LINEARS
+    ctx = vtq.Context(local)
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    ctx.set_stream(stream.cuda_stream)
+    host_w = {nm: synth.weight(vtq.Q4_K, f"c5.{nm}", r, n) for nm, n, r in lins}
+    host_x = {n: synth.activation(f"c5.x.{n}", M, n) for n in sorted({n for _, n, _ in lins})}
+    ranges = {nm: shard.row_range(r, world, rank) for nm, n, r in lins}
+    wbytes = sum((ranges[nm][1] - ranges[nm][0]) * vtq.row_bytes(vtq.Q4_K, n) for nm, n, r in lins)
+    copies = max(1, -(-ROTATE_MIN_BYTES // wbytes))
+    weights = [{nm: ctx.upload(vtq.Q4_K, host_w[nm], n, r, *ranges[nm]) for nm, n, r in lins}
+               for _ in range(copies)]
+    xs = {n: torch.from_numpy(x).cuda() for n, x in host_x.items()}
+    ys = {nm: torch.empty(M * (ranges[nm][1] - ranges[nm][0]), device="cuda") for nm, n, r in lins}
+    full = {nm: torch.empty(world * M * (r // world), device="cuda") for nm, n, r in lins} \
+        if world > 1 else None
+
+    def step(c, events=None):
+        for i, (nm, n, r) in enumerate(lins):
+            if events is not None:
+                events[i][0].record(stream)
+            ctx.linear_ptr(weights[c][nm], xs[n].data_ptr(), ys[nm].data_ptr(), M)
+            if events is not None:
+                events[i][1].record(stream)
+            if world > 1:
+                dist.all_gather_into_tensor(full[nm], ys[nm])
+
+    for c in range(copies):
+        step(c)
+    torch.cuda.synchronize()
+    if args.check and world == 1:
+        from oracle import oracle as O
+        nm, n, r = lins[1]
+        ref = O.linear("q4_k_integer", host_x[n], host_w[nm], M, n, r, os.cpu_count())
+        got = ys[nm].cpu().numpy()
+        assert np.array_equal(got.view(np.uint32), ref.view(np.uint32)), "parity failure"
+    steps = max(1, min(args.steps, 200))
+    warm = max(3, min(args.warmup, 20))
+    for i in range(warm):
+        step(i % copies)
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(steps):
+        step(i % copies)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    ops = prefill_ops(M, lins)
+    value = ops * steps / (ms / 1e3) / 1e12
+    # Per-launch device time of the linears (quantise + GEMM kernels).
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in lins]
+    tot = [0.0] * len(lins)
+    reps = 5
+    for k in range(reps):
+        step(k % copies, evs)
+        torch.cuda.synchronize()
+        for i, (a, b) in enumerate(evs):
+            tot[i] += a.elapsed_time(b)
+    local_ops = sum(2 * M * n * (ranges[nm][1] - ranges[nm][0]) for nm, n, r in lins)
+    achieved = local_ops * reps / (sum(tot) / 1e3) / 1e12
+    peak, peak_src = int8_peak_tops()
+    # e2e: host buffers through the C ABI (x copied in, y copied out per linear).
+    px = {n: torch.from_numpy(x).pin_memory() for n, x in host_x.items()}
+    py = {nm: torch.empty(M * (ranges[nm][1] - ranges[nm][0]), dtype=torch.float32).pin_memory()
+          for nm, n, r in lins}
+    e2e_steps = max(3, min(20, steps))
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(stream)
+    for s_ in range(e2e_steps):
+        for nm, n, r in lins:
+            ctx.linear_ptr(weights[s_ % copies][nm], px[n].data_ptr(), py[nm].data_ptr(), M,
+                           host=True)
+    f1.record(stream)
+    torch.cuda.synchronize()
+    ems = f0.elapsed_time(f1)
+    if world > 1:
+        t = torch.tensor([ems], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ems = float(t.item())
+    e2e = ops * e2e_steps / (ems / 1e3) / 1e12 if world == 1 else \
+        local_ops * world * e2e_steps / (ems / 1e3) / 1e12
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = prefill_cpu_sample()
+    if rank == 0:
+        print(json.dumps({
+            "metric": METRIC, "value": round(value, 2), "unit": "TOPS", "n_gpus": world,
+            "steps": steps, "warmup": warm, "ms_per_step": round(ms / steps, 4),
+            "higher_is_better": True, "scaling": "strong" if world > 1 else "weak",
+            "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "config": {"workload": synth.PREFILL_CFG, "tokens": M,
+                       "linears": [f"Q4_K {n}->{r}" for _, n, r in lins],
+                       "parallelism": f"rows sharded x{world} + NCCL all-gather" if world > 1
+                       else "1 GPU",
+                       "l2": f"{copies} rotating weight copies ({copies * wbytes / 1e6:.0f} MB)",
+                       "ops_per_step": ops},
+            "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": round(peak, 1),
+                         "unit": "TOPS", "frac": round(achieved / peak, 4), "traffic": None,
+                         "peak_source": peak_src, "kernel": "kq_gemm_kernel + quantize_rows",
+                         "ops_per_step_local": local_ops},
+            "e2e": {"value": round(e2e, 2), "unit": "TOPS",
+                    "h2d_bytes_per_step": sum(4 * M * n for _, n, _ in lins),
+                    "d2h_bytes_per_step": sum(4 * M * (ranges[nm][1] - ranges[nm][0])
+                                              for nm, n, r in lins)},
+            "gpu_launches": steps * len(lins) * 2, "clocks": clk, "cpu_baseline": cpu}),
+            flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def prefill_cpu_sample(reps=1):
+    """Oracle linear_q4_k_integer_parallel on the host cores: wk (4096 -> 1024) at
+    M = 512, the bounded sample of config 5."""
+    from vtq import synth
+    from oracle import oracle as O
+    import vtq
+    M = synth.PREFILL_M
+    nm, n, r = synth.PREFILL_LINEARS[1]
+    w = synth.weight(vtq.Q4_K, f"c5.{nm}", r, n)
+    x = synth.activation(f"c5.x.{n}", M, n)
+    threads = os.cpu_count() or 1
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        O.linear("q4_k_integer", x, w, M, n, r, threads)
+    el = time.perf_counter() - t0
+    return {"value": round(2 * M * n * r * reps / el / 1e12, 5), "unit": "TOPS", "cores": threads,
+            "kind": "port", "sample": f"{reps} x wk (Q4_K {n}->{r}) at M={M} in {el:.1f} s, "
+                                      f"{threads} threads (oracle linear_q4_k_integer_parallel)"}
 
 
 def decode_bytes_per_token(cfg, n_pos):
@@ -312,6 +518,9 @@ def main():
 
     if args.impl == "reference":
         run_reference(args, world, rank)
+        return
+    if args.config == PREFILL_CFG_NAME:
+        run_prefill(args, world, rank, local)
         return
     if args.config == DECODE_CFG:
         run_decode(args, world, rank, local)

@@ -13,13 +13,15 @@
 // Tensor-core mapping. For one superblock s both integers are contractions
 // over its 256 positions k, so they are computed as one MMA product of the
 // activation tile (A: 128 tokens x 256 int8, K-major) with three unsigned
-// byte planes of the weights (B: 96 "rows" x 256):
-//   rows  0..31  lo_k = (sc_j(k) * q_k) & 127
-//   rows 32..63  hi_k = (sc_j(k) * q_k) >> 7          (sc * q <= 945 < 1024)
+// byte planes of the weights (B: 96 "rows" x 256). With sc = 8 sh + sl
+// (sh, sl in [0, 7]):
+//   rows  0..31  lo_k = sl_j(k) * q_k                 (<= 105)
+//   rows 32..63  hi_k = sh_j(k) * q_k                 (<= 105)
 //   rows 64..95  mn_j(k)                              (the 6-bit min, repeated)
-// so acc = D[:, r] + 128 * D[:, 32 + r] and acc_m = D[:, 64 + r] exactly
-// (|acc| <= 256 * 127 * 945 < 2^31). The planes are built in shared memory
-// from the packed superblocks by two builder warps; the per-superblock fp
+// so acc = D[:, r] + 8 * D[:, 32 + r] and acc_m = D[:, 64 + r] exactly
+// (|acc| <= 256 * 127 * 945 < 2^31). Every byte product stays below 256, so
+// one 32-bit multiply scales four packed quants at once. The planes are built
+// in shared memory from the packed superblocks by two builder warps; the per-superblock fp
 // combine and the cross-superblock fixed_tree stay on CUDA cores, in the
 // reference's op order, with the tree kept per (token, row) in registers as a
 // binary counter of complete subtrees (identical pairings to the level-wise
@@ -29,7 +31,7 @@
 //   warp 0      TMA producer: activation tile (2 x 16 KB, 128B-swizzled) and
 //               the 32 rows' superblock (32 x 144 B) per step
 //   warp 1      TMEM owner; lane 0 issues 8 MMAs (K = 32 each) per step
-//   warps 2-3   plane builders (64 threads: one row x one 128-position half)
+//   warps 2-3   plane builders (64 threads: one row x two pairs of sub-blocks)
 //   warps 4-11  epilogue: TMEM -> registers, fp combine, fixed_tree
 // Every wait is bounded (%globaltimer); a timeout sets the status word, stops
 // the pipeline and still frees TMEM.
@@ -74,7 +76,7 @@ struct GemmParams {
   int M, n, S, R;
   float* y;
   int64_t ldy;
-  const float* xd;  // [M][S] activation block scales
+  const float* xd;  // [S][M] activation block scales (token-major per superblock)
   unsigned* status;
 };
 
@@ -145,16 +147,34 @@ __device__ __forceinline__ uint32_t plane_off(int nr, int k) {
   return (uint32_t)(kb * P_KBLK + (nr >> 3) * 1024 + (nr & 7) * 128 + ((chunk ^ (nr & 7)) << 4));
 }
 
-// sc * q for the four nibble bytes of `nib`, split into (low 7 bits, high bits).
-__device__ __forceinline__ void scale_split(uint32_t nib, uint32_t sc, uint32_t& lo, uint32_t& hi) {
-  const uint32_t pe = (nib & 0x00FF00FFu) * sc;          // bytes 0 and 2 in 16-bit lanes
-  const uint32_t po = ((nib >> 8) & 0x00FF00FFu) * sc;   // bytes 1 and 3
-  lo = (pe & 0x007F007Fu) | ((po & 0x007F007Fu) << 8);
-  hi = ((pe >> 7) & 0x00070007u) | (((po >> 7) & 0x00070007u) << 8);
-}
-
 __device__ __forceinline__ float h2f(uint32_t bits) {
   return __half2float(__ushort_as_half((unsigned short)bits));
+}
+
+// Push leaf values v into the per-pair binary counters: merge with levels
+// 0..tz-1 (older subtree on the left), store at level tz.
+template <int LV, int TZ>
+__device__ __forceinline__ void tree_push_tz(float (&st)[LV][16], float (&v)[16]) {
+#pragma unroll
+  for (int i = 0; i < 16; i++) {
+    float c = v[i];
+#pragma unroll
+    for (int L = 0; L < TZ; L++) c = __fadd_rn(st[L][i], c);
+    st[TZ][i] = c;
+  }
+}
+
+template <int LV>
+__device__ __forceinline__ void tree_push(float (&st)[LV][16], float (&v)[16], int tz) {
+  switch (tz) {
+    case 0: tree_push_tz<LV, 0>(st, v); break;
+    case 1: tree_push_tz<LV, 1>(st, v); break;
+    case 2: tree_push_tz<LV, 2>(st, v); break;
+    case 3: tree_push_tz<LV, (3 < LV ? 3 : LV - 1)>(st, v); break;
+    case 4: tree_push_tz<LV, (4 < LV ? 4 : LV - 1)>(st, v); break;
+    case 5: tree_push_tz<LV, (5 < LV ? 5 : LV - 1)>(st, v); break;
+    default: tree_push_tz<LV, LV - 1>(st, v); break;
+  }
 }
 
 template <int LV>
@@ -251,8 +271,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else if (warp < 2 + kBuildWarps) {
-    // ---- plane builders: thread = (row r, K-block kb) ----
-    const int t = tid - 64, r = t >> 1, kb = t & 1;
+    // ---- plane builders: thread = (row r, K-block kb = sub-blocks 4 kb ..
+    // 4 kb + 3); 8 consecutive lanes take 8 consecutive rows so that their
+    // 16-byte plane stores land in 8 different swizzled slots of a line ----
+    const int t = tid - 64, r = t & 31, kb = t >> 5;
     for (int s = 0; s < S && !*abort_flag; s++) {
       const int sw = s % NW, sp = s % NP, sm = s % NMETA;
       if (!wait_u32(W_FULL(sw), (s / NW) & 1) || !wait_u32(P_EMPTY(sp), ((s / NP) + 1) & 1) ||
@@ -265,36 +287,45 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint8_t* pl = gbase + OFF_P + sp * P_STAGE;
       if (kb == 0) meta[sm * GR + r] = make_float2(h2f(hdr.x & 0xffffu), h2f(hdr.x >> 16));
 #pragma unroll
-      for (int jj = 0; jj < 4; jj++) {
-        const int j = 4 * kb + jj;  // sub-block
-        // get_scale_min_k4 (quant.rs:268-276)
-        uint32_t sc, mn;
+      for (int jp = 2 * kb; jp < 2 * kb + 2; jp++) {
+      // get_scale_min_k4 (quant.rs:268-276) for sub-blocks 2 jp (low nibbles)
+      // and 2 jp + 1 (high nibbles of the same 32 bytes).
+      uint32_t sc[2], mn[2];
+#pragma unroll
+      for (int e = 0; e < 2; e++) {
+        const int j = 2 * jp + e;
         if (j < 4) {
-          sc = (hdr.y >> (8 * j)) & 63;
-          mn = (hdr.z >> (8 * j)) & 63;
+          sc[e] = (hdr.y >> (8 * j)) & 63;
+          mn[e] = (hdr.z >> (8 * j)) & 63;
         } else {
           const int k4 = j - 4;
           const uint32_t lo4 = (hdr.w >> (8 * k4)) & 0xff;
-          sc = (lo4 & 15) | (((hdr.y >> (8 * k4 + 6)) & 3) << 4);
-          mn = (lo4 >> 4) | (((hdr.z >> (8 * k4 + 6)) & 3) << 4);
+          sc[e] = (lo4 & 15) | (((hdr.y >> (8 * k4 + 6)) & 3) << 4);
+          mn[e] = (lo4 >> 4) | (((hdr.z >> (8 * k4 + 6)) & 3) << 4);
         }
-        const uint32_t mrep = mn * 0x01010101u;
-        const uint8_t* qs = sb + 16 + 32 * (j >> 1);  // pair of sub-blocks sharing bytes
+      }
+      const uint8_t* qs = sb + 16 + 32 * jp;
 #pragma unroll
-        for (int h16 = 0; h16 < 2; h16++) {
-          const uint4 w = *reinterpret_cast<const uint4*>(qs + 16 * h16);
-          const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
+      for (int h16 = 0; h16 < 2; h16++) {
+        const uint4 w = *reinterpret_cast<const uint4*>(qs + 16 * h16);
+        const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int e = 0; e < 2; e++) {
+          const uint32_t sl = sc[e] & 7, sh = sc[e] >> 3;
           uint32_t lo[4], hi[4];
 #pragma unroll
           for (int u = 0; u < 4; u++) {
-            const uint32_t nib = (j & 1) ? ((wv[u] >> 4) & 0x0F0F0F0Fu) : (wv[u] & 0x0F0F0F0Fu);
-            scale_split(nib, sc, lo[u], hi[u]);
+            const uint32_t nib = e ? ((wv[u] >> 4) & 0x0F0F0F0Fu) : (wv[u] & 0x0F0F0F0Fu);
+            lo[u] = nib * sl;  // byte products <= 105: no carries between bytes
+            hi[u] = nib * sh;
           }
-          const int k = 32 * j + 16 * h16;
+          const int k = 32 * (2 * jp + e) + 16 * h16;
+          const uint32_t mrep = mn[e] * 0x01010101u;
           *reinterpret_cast<uint4*>(pl + plane_off(r, k)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
           *reinterpret_cast<uint4*>(pl + plane_off(GR + r, k)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
           *reinterpret_cast<uint4*>(pl + plane_off(2 * GR + r, k)) = make_uint4(mrep, mrep, mrep, mrep);
         }
+      }
       }
       // Generic-proxy stores -> visible to the tensor core (async proxy).
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -314,16 +345,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int L = 0; L < LV; L++)
 #pragma unroll
       for (int i = 0; i < 16; i++) st[L][i] = 0.0f;
-    float xd_next = bvalid ? p.xd[(int64_t)b * S] : 0.0f;
+    float xd_next = bvalid ? p.xd[b] : 0.0f;
     for (int s = 0; s < S && !*abort_flag; s++) {
       const int ab = s & 1, sm = s % NMETA;
       const float xdv = xd_next;
-      if (s + 1 < S) xd_next = bvalid ? p.xd[(int64_t)b * S + s + 1] : 0.0f;
+      if (s + 1 < S) xd_next = bvalid ? p.xd[(int64_t)(s + 1) * p.M + b] : 0.0f;
       if (!wait_u32(A_FULL(ab), (s >> 1) & 1) || !wait_u32(M_FULL(sm), (s / NMETA) & 1)) {
         if (lane == 0) fail();
         break;
       }
       tc_fence_after();
+      float part[16];
 #pragma unroll
       for (int hh = 0; hh < 2; hh++) {
         const int rr = rbase + 8 * hh;
@@ -336,26 +368,16 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int i = 0; i < 8; i++) {
           const float2 dm = meta[sm * GR + rr + i];
-          const int acc = vlo[i] + (vhi[i] << 7);
+          const int acc = vlo[i] + (vhi[i] << 3);
           const float t0 = __fmul_rn(__fmul_rn(dm.x, xdv), __int2float_rn(acc));
           const float t1 = __fmul_rn(__fmul_rn(dm.y, xdv), __int2float_rn(vmn[i]));
-          float carry = __fsub_rn(t0, t1);
-          // Binary counter over superblocks: level L holds a complete subtree
-          // of 2^L leaves while bit L of the number of leaves seen is set.
-          bool done = false;
-#pragma unroll
-          for (int L = 0; L < LV; L++) {
-            if (!done) {
-              if ((s >> L) & 1) {
-                carry = __fadd_rn(st[L][8 * hh + i], carry);
-              } else {
-                st[L][8 * hh + i] = carry;
-                done = true;
-              }
-            }
-          }
+          part[8 * hh + i] = __fsub_rn(t0, t1);
         }
       }
+      // Binary counter over superblocks: level L holds a complete subtree of
+      // 2^L leaves while bit L of the number of leaves seen (s) is set. Leaf s
+      // merges with the levels below the lowest clear bit of s (warp-uniform).
+      tree_push<LV>(st, part, __ffs(~s) - 1);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {
@@ -391,7 +413,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // quantize_block_q8 (quant.rs:750-771) for every (row, 256-block): one warp
 // per block, 8 contiguous elements per lane; int8 codes to xq [M][n], block
-// scales to xd [M][S].
+// scales to xd [S][M].
 __global__ void quantize_rows_kernel(const float* __restrict__ x, int64_t ldx, int M, int n,
                                      int8_t* __restrict__ xq, float* __restrict__ xd) {
   const int S = n / 256;
@@ -420,7 +442,7 @@ __global__ void quantize_rows_kernel(const float* __restrict__ x, int64_t ldx, i
     else w1 |= (uint32_t)(qv & 0xff) << (8 * (i - 4));
   }
   *reinterpret_cast<uint2*>(xq + (int64_t)b * n + 256 * s + 8 * lane) = make_uint2(w0, w1);
-  if (lane == 0) xd[(int64_t)b * S + s] = d;
+  if (lane == 0) xd[(int64_t)s * M + b] = d;
 }
 
 typedef CUresult (*EncodeFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,

@@ -164,3 +164,12 @@ CONFIGS = {
     "c2_q4_k_llama7b_ffn": [(Q4_K, 4096, 11008), (Q4_K, 11008, 4096)],
     "c3_q6_k_head_4096x32000": [(Q6_K, 4096, 32000)],
 }
+
+# Config 5: one Mistral-7B layer's linears (wq, wk, wv, wo, w1, w3, w2) as
+# batched Q4_K products at M = 512 prompt tokens.
+PREFILL_CFG = "c5_q4_k_prefill_mistral"
+PREFILL_M = 512
+PREFILL_LINEARS = [  # (name, in_feat, out_feat)
+    ("wq", 4096, 4096), ("wk", 4096, 1024), ("wv", 4096, 1024), ("wo", 4096, 4096),
+    ("w1", 4096, 14336), ("w3", 4096, 14336), ("w2", 14336, 4096),
+]
