@@ -21,7 +21,7 @@
 // so acc = D[:, r] + 8 * D[:, 32 + r] and acc_m = D[:, 64 + r] exactly
 // (|acc| <= 256 * 127 * 945 < 2^31). Every byte product stays below 256, so
 // one 32-bit multiply scales four packed quants at once. The planes are built
-// in shared memory from the packed superblocks by two builder warps; the per-superblock fp
+// in shared memory from the packed superblocks by four builder warps; the per-superblock fp
 // combine and the cross-superblock fixed_tree stay on CUDA cores, in the
 // reference's op order, with the tree kept per (token, row) in registers as a
 // binary counter of complete subtrees (identical pairings to the level-wise
@@ -31,8 +31,8 @@
 //   warp 0      TMA producer: activation tile (2 x 16 KB, 128B-swizzled) and
 //               the 32 rows' superblock (32 x 144 B) per step
 //   warp 1      TMEM owner; lane 0 issues 8 MMAs (K = 32 each) per step
-//   warps 2-3   plane builders (64 threads: one row x two pairs of sub-blocks)
-//   warps 4-11  epilogue: TMEM -> registers, fp combine, fixed_tree
+//   warps 4-7   plane builders (128 threads: one row x one pair of sub-blocks)
+//   warps 8-15  epilogue: TMEM -> registers, fp combine, fixed_tree
 // Every wait is bounded (%globaltimer); a timeout sets the status word, stops
 // the pipeline and still frees TMEM.
 #include <cuda.h>
@@ -50,17 +50,22 @@ namespace {
 constexpr int GM = 128;         // tokens per CTA = MMA M = TMEM lanes
 constexpr int GR = 32;          // weight rows per CTA
 constexpr int GN = 3 * GR;      // MMA N: lo | hi | mins
-constexpr int NX = 3;           // activation stages
+constexpr int NX = 4;           // activation stages
 constexpr int NW = 4;           // packed-weight stages
-constexpr int NP = 2;           // plane stages
+constexpr int NP = 3;           // plane stages
+constexpr int NA = 3;           // TMEM accumulator buffers (128 columns apart)
 constexpr int NMETA = 4;        // d / dmin stages
 constexpr uint32_t X_STAGE = GM * 256;  // 2 K-blocks x 16 KB
 constexpr uint32_t P_STAGE = GN * 256;  // 2 K-blocks x 12 KB
 constexpr uint32_t P_KBLK = GN * 128;
 constexpr uint32_t W_STAGE = GR * 144;
-constexpr uint32_t TMEM_COLS = 256;     // two accumulator buffers of GN columns
-constexpr int kBuildWarps = 2, kEpiWarps = 8;
-constexpr int kThreads = 32 * (2 + kBuildWarps + kEpiWarps);
+constexpr uint32_t TMEM_COLS = 512;     // NA accumulator buffers of GN columns
+constexpr int kBuildWarps = 4, kEpiWarps = 8;
+// Warpgroups: 0 = producer, MMA issuer, two idle warps; 1 = builders;
+// 2-3 = epilogue. Registers are re-split per warpgroup with setmaxnreg
+// (sum 128*56 + 128*80 + 256*184 = 64512 <= 512 threads * 128 at launch).
+constexpr int kThreads = 512;
+constexpr int kBuildWarp0 = 4, kEpiWarp0 = 8;
 
 // Shared-memory map (offsets from a 1024-aligned base).
 constexpr uint32_t OFF_X = 0;
@@ -68,9 +73,20 @@ constexpr uint32_t OFF_P = OFF_X + NX * X_STAGE;
 constexpr uint32_t OFF_W = OFF_P + NP * P_STAGE;
 constexpr uint32_t OFF_META = OFF_W + NW * W_STAGE;
 constexpr uint32_t OFF_BAR = OFF_META + NMETA * GR * 8;
-constexpr int NBAR = 2 * (NX + NW + NP + NMETA + 2);
+constexpr int NBAR = 2 * (NX + NW + NP + NMETA + NA);
+static_assert(NA * 128 <= (int)TMEM_COLS, "accumulator buffers exceed the TMEM allocation");
 constexpr uint32_t OFF_SLOT = OFF_BAR + NBAR * 8;
 constexpr uint32_t SMEM_BYTES = OFF_SLOT + 16 + 1024;  // + alignment slack
+
+#ifdef VTQ_GEMM_TRACE
+__device__ long long g_gemm_trace[64][8];
+#define GT(slot, s_)                                                              \
+  do {                                                                            \
+    if (blockIdx.x == 0 && blockIdx.y == 1 && (s_) < 64) g_gemm_trace[s_][slot] = clock64(); \
+  } while (0)
+#else
+#define GT(slot, s_) (void)0
+#endif
 
 struct GemmParams {
   int M, n, S, R;
@@ -194,7 +210,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   auto M_FULL = [&](int i) { return bar0 + 8u * (2 * NX + 2 * NW + 2 * NP + i); };
   auto M_EMPTY = [&](int i) { return bar0 + 8u * (2 * NX + 2 * NW + 2 * NP + NMETA + i); };
   auto A_FULL = [&](int i) { return bar0 + 8u * (2 * NX + 2 * NW + 2 * NP + 2 * NMETA + i); };
-  auto A_EMPTY = [&](int i) { return bar0 + 8u * (2 * NX + 2 * NW + 2 * NP + 2 * NMETA + 2 + i); };
+  auto A_EMPTY = [&](int i) { return bar0 + 8u * (2 * NX + 2 * NW + 2 * NP + 2 * NMETA + NA + i); };
   volatile uint32_t* slot = reinterpret_cast<volatile uint32_t*>(gbase + OFF_SLOT);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(gbase + OFF_SLOT + 4);
   float2* meta = reinterpret_cast<float2*>(gbase + OFF_META);
@@ -211,7 +227,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int i = 0; i < NW; i++) { init(W_FULL(i), 1); init(W_EMPTY(i), 32 * kBuildWarps); }
     for (int i = 0; i < NP; i++) { init(P_FULL(i), 32 * kBuildWarps); init(P_EMPTY(i), 1); }
     for (int i = 0; i < NMETA; i++) { init(M_FULL(i), 32 * kBuildWarps); init(M_EMPTY(i), kEpiWarps); }
-    for (int i = 0; i < 2; i++) { init(A_FULL(i), 1); init(A_EMPTY(i), kEpiWarps); }
+    for (int i = 0; i < NA; i++) { init(A_FULL(i), 1); init(A_EMPTY(i), kEpiWarps); }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -231,6 +247,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   };
 
   if (warp == 0) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 56;");
     // ---- producer ----
     if (lane == 0) {
       for (int s = 0; s < S && !*abort_flag; s++) {
@@ -244,19 +261,25 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_arrive_expect_tx(reinterpret_cast<uint64_t*>(gbase + OFF_BAR + 8 * (2 * NX + sw)),
                               W_STAGE);
         tma_load_2d(base + OFF_W + sw * W_STAGE, &tmw, 144 * s, row0, W_FULL(sw));
+        GT(0, s);
       }
     }
   } else if (warp == 1) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 56;");
     // ---- MMA issuer ----
     if (lane == 0) {
       for (int s = 0; s < S && !*abort_flag; s++) {
-        const int sx = s % NX, sp = s % NP, ab = s & 1;
-        if (!wait_u32(X_FULL(sx), (s / NX) & 1) || !wait_u32(P_FULL(sp), (s / NP) & 1) ||
-            !wait_u32(A_EMPTY(ab), ((s >> 1) + 1) & 1)) {
+        const int sx = s % NX, sp = s % NP, ab = s % NA;
+        bool ok = wait_u32(X_FULL(sx), (s / NX) & 1);
+        GT(6, s);
+        ok = ok && wait_u32(P_FULL(sp), (s / NP) & 1);
+        GT(7, s);
+        if (!ok || !wait_u32(A_EMPTY(ab), ((s / NA) + 1) & 1)) {
           fail();
           break;
         }
         tc_fence_after();
+        GT(2, s);
         const uint32_t xs = base + OFF_X + sx * X_STAGE, ps = base + OFF_P + sp * P_STAGE;
         const uint32_t d = tmem + (uint32_t)ab * 128u;
 #pragma unroll
@@ -270,13 +293,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         mma_commit(A_FULL(ab));
       }
     }
-  } else if (warp < 2 + kBuildWarps) {
-    // ---- plane builders: thread = (row r, K-block kb = sub-blocks 4 kb ..
-    // 4 kb + 3); 8 consecutive lanes take 8 consecutive rows so that their
-    // 16-byte plane stores land in 8 different swizzled slots of a line ----
-    const int t = tid - 64, r = t & 31, kb = t >> 5;
+  } else if (warp < kBuildWarp0) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 56;");  // idle
+  } else if (warp < kEpiWarp0) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 80;");
+    // ---- plane builders: thread = (row r, sub-block pair jp = 2 jp, 2 jp + 1);
+    // 8 consecutive lanes take 8 consecutive rows so that their 16-byte plane
+    // stores land in 8 different swizzled slots of a 128-byte line ----
+    const int t = tid - 32 * kBuildWarp0, r = t & 31, jp = t >> 5;
     for (int s = 0; s < S && !*abort_flag; s++) {
       const int sw = s % NW, sp = s % NP, sm = s % NMETA;
+      if (t == 0) GT(5, s);
       if (!wait_u32(W_FULL(sw), (s / NW) & 1) || !wait_u32(P_EMPTY(sp), ((s / NP) + 1) & 1) ||
           !wait_u32(M_EMPTY(sm), ((s / NMETA) + 1) & 1)) {
         fail();
@@ -285,9 +312,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint8_t* sb = gbase + OFF_W + sw * W_STAGE + r * 144;
       const uint4 hdr = *reinterpret_cast<const uint4*>(sb);
       uint8_t* pl = gbase + OFF_P + sp * P_STAGE;
-      if (kb == 0) meta[sm * GR + r] = make_float2(h2f(hdr.x & 0xffffu), h2f(hdr.x >> 16));
-#pragma unroll
-      for (int jp = 2 * kb; jp < 2 * kb + 2; jp++) {
+      if (jp == 0) meta[sm * GR + r] = make_float2(h2f(hdr.x & 0xffffu), h2f(hdr.x >> 16));
+      {
       // get_scale_min_k4 (quant.rs:268-276) for sub-blocks 2 jp (low nibbles)
       // and 2 jp + 1 (high nibbles of the same 32 bytes).
       uint32_t sc[2], mn[2];
@@ -329,13 +355,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       // Generic-proxy stores -> visible to the tensor core (async proxy).
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      if (t == 0) GT(1, s);
       mbar_arrive(P_FULL(sp));
       mbar_arrive(M_FULL(sm));
       mbar_arrive(W_EMPTY(sw));
     }
   } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 184;");
     // ---- epilogue: thread = token (TMEM lane), 16 weight rows ----
-    const int ew = warp - (2 + kBuildWarps);
+    const int ew = warp - kEpiWarp0;
     const int q = warp & 3, half = ew >> 2;
     const int b = tok0 + 32 * q + lane;
     const bool bvalid = b < p.M;
@@ -347,14 +375,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int i = 0; i < 16; i++) st[L][i] = 0.0f;
     float xd_next = bvalid ? p.xd[b] : 0.0f;
     for (int s = 0; s < S && !*abort_flag; s++) {
-      const int ab = s & 1, sm = s % NMETA;
+      const int ab = s % NA, sm = s % NMETA;
       const float xdv = xd_next;
       if (s + 1 < S) xd_next = bvalid ? p.xd[(int64_t)(s + 1) * p.M + b] : 0.0f;
-      if (!wait_u32(A_FULL(ab), (s >> 1) & 1) || !wait_u32(M_FULL(sm), (s / NMETA) & 1)) {
+      if (!wait_u32(A_FULL(ab), (s / NA) & 1) || !wait_u32(M_FULL(sm), (s / NMETA) & 1)) {
         if (lane == 0) fail();
         break;
       }
       tc_fence_after();
+      if (ew == 0 && lane == 0) GT(3, s);
       float part[16];
 #pragma unroll
       for (int hh = 0; hh < 2; hh++) {
@@ -378,6 +407,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // 2^L leaves while bit L of the number of leaves seen (s) is set. Leaf s
       // merges with the levels below the lowest clear bit of s (warp-uniform).
       tree_push<LV>(st, part, __ffs(~s) - 1);
+      if (ew == 0 && lane == 0) GT(4, s);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {
