@@ -500,6 +500,177 @@ def run_decode(args, world, rank, local):
         dist.destroy_process_group()
 
 
+def run_sharded(args, world, rank, local, ctx, stream, cfg):
+    """N > 1: every matvec's output rows are split into contiguous ranges, one per
+    rank; a step is the local matvec plus an NCCL all-gather of y over NVLink
+    (strong scaling: the job's total work is the N = 1 workload)."""
+    import torch
+    import torch.distributed as dist
+    import vtq
+    from vtq import synth, shard
+    host_w = [synth.weight(dt, f"{args.config}.w.{n}x{r}", r, n) for dt, n, r in cfg]
+    host_x = [synth.activation(f"{args.config}.x.{n}", 1, n) for dt, n, r in cfg]
+    rng = [shard.row_range(r, world, rank) for dt, n, r in cfg]
+    for (dt, n, r) in cfg:
+        if r % world:
+            raise SystemExit(f"{args.config}: {r} rows do not split evenly over {world} ranks")
+    wbytes = sum((b - a) * vtq.row_bytes(dt, n) for (dt, n, r), (a, b) in zip(cfg, rng))
+    copies = max(1, -(-ROTATE_MIN_BYTES // wbytes))
+    weights = [[ctx.upload(dt, host_w[i], n, r, *rng[i]) for i, (dt, n, r) in enumerate(cfg)]
+               for _ in range(copies)]
+    xs = [torch.from_numpy(x).cuda() for x in host_x]
+    ys = [torch.empty(b - a, device="cuda") for a, b in rng]
+    fused = all(dt in (vtq.Q4_K, vtq.Q6_K) for dt, n, r in cfg) and world <= 8 and \
+        os.environ.get("VTQ_GATHER", "fused") == "fused"
+    offs = [sum(r for _, _, r in cfg[:i]) for i in range(len(cfg))]
+    if fused:
+        # Fused path: each matvec stores its rows into every rank's full y over
+        # NVLink; one bounded wait per step for world x len(cfg) arrivals.
+        gat = vtq.Gather(ctx, sum(r for _, _, r in cfg))
+        full = [device_view(gat.y_ptr + 4 * offs[i], r) for i, (dt, n, r) in enumerate(cfg)]
+    else:
+        full = [torch.empty(r, device="cuda") for dt, n, r in cfg]
+
+    def step(c):
+        for i in range(len(cfg)):
+            if fused:
+                gat.linear(weights[c][i], xs[i].data_ptr(), rng[i][0], cfg[i][2], offs[i])
+            else:
+                ctx.linear_ptr(weights[c][i], xs[i].data_ptr(), ys[i].data_ptr(), 1)
+                dist.all_gather_into_tensor(full[i], ys[i])
+        if fused:
+            gat.wait(world * len(cfg))
+
+    for c in range(copies):
+        step(c)
+    torch.cuda.synchronize()
+    # Shard invariance: the gathered y equals the oracle's full y bit for bit.
+    from oracle import oracle as O
+    for i, (dt, n, r) in enumerate(cfg):
+        name = {12: "q4_k_integer", 14: "q6_k_integer"}.get(dt)
+        ref = O.linear(name, host_x[i], host_w[i], 1, n, r, os.cpu_count()) if name else \
+            O.linear_dispatch(dt, host_x[i], host_w[i], n, r, threads=os.cpu_count())
+        got = full[i].cpu().numpy()
+        if not np.array_equal(got.view(np.uint32), ref.view(np.uint32)):
+            raise SystemExit(f"rank {rank}: sharded result differs from the oracle ({args.config})")
+    steps = max(copies, min(args.steps, 2000)) // copies * copies
+    for i in range(max(3, args.warmup)):
+        step(i % copies)
+    torch.cuda.synchronize()
+    graph = None
+    if fused:
+        # One rotation (copies steps) as a CUDA graph, replayed.
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream, capture_error_mode="thread_local"):
+            for c in range(copies):
+                step(c)
+        graph.replay()
+        torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    dist.barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    if graph is not None:
+        for _ in range(steps // copies):
+            graph.replay()
+    else:
+        for i in range(steps):
+            step(i % copies)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    dist.barrier()
+    ms = torch.tensor([e0.elapsed_time(e1)], device="cuda")
+    dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    ms = float(ms.item())
+    step_bytes = sum(algo_bytes(dt, n, r) for dt, n, r in cfg)
+    value = step_bytes * steps / (ms / 1e3) / 1e9
+    # Local kernel time alone (no collective), for the roofline of the shard.
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in cfg]
+    durs = []
+    for k in range(50):
+        for i in range(len(cfg)):
+            evs[i][0].record(stream)
+            ctx.linear_ptr(weights[k % copies][i], xs[i].data_ptr(), ys[i].data_ptr(), 1)
+            evs[i][1].record(stream)
+        torch.cuda.synchronize()
+        durs += [a.elapsed_time(b) for a, b in evs]
+    local_bytes = statistics.mean(
+        (b - a) * vtq.row_bytes(dt, n) + 4 * n + 4 * (b - a) for (dt, n, r), (a, b) in zip(cfg, rng))
+    peak, peak_kind = peaks()
+    achieved = local_bytes / (statistics.mean(durs) / 1e3) / 1e9
+    gather_bytes = sum(4 * r for dt, n, r in cfg)
+    # e2e: pinned host x -> device, local matvec, all-gather, full y -> pinned host.
+    px = [torch.from_numpy(x).pin_memory() for x in host_x]
+    py = [torch.empty(r, dtype=torch.float32).pin_memory() for dt, n, r in cfg]
+    e2e_steps = max(20, min(1000, steps // 2))
+    dist.barrier()
+    torch.cuda.synchronize()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(stream)
+    for k in range(e2e_steps):
+        for i in range(len(cfg)):
+            xs[i].copy_(px[i], non_blocking=True)
+            if fused:
+                gat.linear(weights[k % copies][i], xs[i].data_ptr(), rng[i][0], cfg[i][2], offs[i])
+            else:
+                ctx.linear_ptr(weights[k % copies][i], xs[i].data_ptr(), ys[i].data_ptr(), 1)
+                dist.all_gather_into_tensor(full[i], ys[i])
+        if fused:
+            gat.wait(world * len(cfg))
+        for i in range(len(cfg)):
+            py[i].copy_(full[i], non_blocking=True)
+    f1.record(stream)
+    torch.cuda.synchronize()
+    ems = torch.tensor([f0.elapsed_time(f1)], device="cuda")
+    dist.all_reduce(ems, op=dist.ReduceOp.MAX)
+    e2e = {"value": round(step_bytes * e2e_steps / (float(ems.item()) / 1e3) / 1e9, 2),
+           "unit": "GB/s", "h2d_bytes_per_step": sum(4 * n for dt, n, r in cfg),
+           "d2h_bytes_per_step": sum(4 * r for dt, n, r in cfg), "steps": e2e_steps}
+    if rank == 0:
+        print(json.dumps({
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+            "steps": steps, "warmup": max(3, args.warmup), "ms_per_step": round(ms / steps, 5),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8",
+            "data": "synthetic",
+            "config": {"workload": args.config,
+                       "matvecs": [f"{vtq.formats.NAMES[dt]} {n}->{r}" for dt, n, r in cfg],
+                       "batch": 1, "parallelism": f"rows sharded x{world} + " + ("fused NVLink all-gather (each matvec stores its rows into every rank's y)" if fused else "NCCL all-gather of y"),
+                       "l2": f"inputs larger than L2: {copies} rotating weight copies per rank "
+                             f"({copies * wbytes / 1e6:.0f} MB)",
+                       "timing": ("CUDA graph of one rotation (fused matvec+gather kernels and the "
+                                  "arrival wait), replayed" if fused else
+                                  "eager launches (kernel + all_gather per matvec)") +
+                                 "; CUDA events, max over ranks"},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                         "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": None,
+                         "peak_source": peak_kind, "kernel": "kq_matvec_kernel (local shard)",
+                         "bytes_per_launch": local_bytes,
+                         "avg_launch_us": round(1e3 * statistics.mean(durs), 3)},
+            "nvlink": {"all_gather_bytes_per_step": gather_bytes},
+            "parity": "gathered y bit-identical to the oracle on every rank",
+            "e2e": e2e, "gpu_launches": steps * len(cfg), "clocks": clk,
+            "cpu_baseline": None}), flush=True)
+    if fused:
+        torch.cuda.synchronize()
+        dist.barrier()
+        gat.close()
+    dist.destroy_process_group()
+
+
+def device_view(ptr, n):
+    """A float32 torch view of n floats at device address ptr (no copy)."""
+    import torch
+
+    class _A:
+        __cuda_array_interface__ = {"shape": (n,), "typestr": "<f4", "data": (ptr, False),
+                                    "version": 3}
+    return torch.as_tensor(_A(), device="cuda")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -540,6 +711,9 @@ def main():
     ctx.set_stream(stream.cuda_stream)
 
     cfg = synth.CONFIGS[args.config]
+    if world > 1:
+        run_sharded(args, world, rank, local, ctx, stream, cfg)
+        return
     step_bytes = sum(algo_bytes(dt, n, r) for dt, n, r in cfg)
     wbytes = sum(r * vtq.row_bytes(dt, n) for dt, n, r in cfg)
     copies = max(1, -(-ROTATE_MIN_BYTES // wbytes))

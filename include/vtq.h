@@ -182,6 +182,28 @@ float vtq_powf(float x, float y);
  * powf(1e4, v/64), powf(1e6, v/64), 1/(1+expf(-v)); out holds 7*n floats. */
 void vtq_libm_sweep(const float* in, size_t n, float* out);
 
+/* ---- Row-sharded linears with the all-gather fused into the kernel ----
+ * No counterpart in the reference (it is single-process; its parallel
+ * linears split output rows over threads, src/ops/quant.rs:1120-1143, which
+ * is the same row split these calls spread over GPUs).
+ * Each rank creates a gather buffer (full y + counters), exports its CUDA IPC
+ * handle (64 bytes), and connects to every rank's handle. vtq_linear_gather
+ * computes this rank's rows [row0, row0 + rows) of y = W x and stores them into
+ * the full y of every rank over NVLink, then signals every rank once;
+ * vtq_gather_wait holds the context's stream until `signals` more rank
+ * launches have arrived (one per rank per gathered linear). Waits are bounded
+ * (2 s) and report VTQ_ERR_TIMEOUT through the context status. */
+typedef struct vtq_gather vtq_gather;
+vtq_status vtq_gather_create(vtq_ctx* ctx, int32_t world, int32_t rank, size_t y_floats,
+                             vtq_gather** out, uint8_t* ipc_handle /* 64 bytes */);
+vtq_status vtq_gather_connect(vtq_gather* g, const uint8_t* handles /* world x 64 bytes */);
+float* vtq_gather_y(vtq_gather* g);
+vtq_status vtq_linear_gather(vtq_ctx* ctx, const vtq_weight* w, const float* x, int64_t batch,
+                             vtq_gather* g, int64_t y_offset, int64_t ldy, int64_t row0,
+                             uint32_t flags);
+vtq_status vtq_gather_wait(vtq_ctx* ctx, vtq_gather* g, uint32_t signals);
+vtq_status vtq_gather_destroy(vtq_gather* g);
+
 #ifdef __cplusplus
 }
 #endif

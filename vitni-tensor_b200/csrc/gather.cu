@@ -1,0 +1,44 @@
+// gather.cu -- completion side of the fused row-shard all-gather.
+//
+// A row-sharded linear (each rank owns a contiguous range of output rows,
+// shard-invariant because every output row is its own reduction,
+// vitni-tensor src/ops/quant.rs:1373-1377) writes its rows straight into the
+// full-y buffer of every rank over NVLink and then adds 1 to every rank's
+// arrival counter (kquant_matvec.cu). This kernel is the receiving side: it
+// holds the stream until the expected number of arrivals has been seen, so
+// that later work on the stream reads a complete y. Counters only grow; the
+// number of arrivals consumed so far lives in device memory next to them, so
+// the wait needs no host-side epoch and can be captured in a CUDA graph.
+#include "vtq_device.cuh"
+#include "vtq_internal.h"
+
+namespace vtq {
+namespace {
+
+__global__ void gather_wait_kernel(const unsigned* cnt, unsigned* expected, unsigned signals,
+                                   unsigned* status) {
+  if (threadIdx.x != 0) return;
+  const unsigned target = *expected + signals;
+  *expected = target;
+  const uint64_t t0 = globaltimer();
+  for (;;) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(cnt) : "memory");
+    if ((int)(v - target) >= 0) break;  // wrap-safe comparison
+    if (globaltimer() - t0 > VTQ_WAIT_LIMIT_NS) {
+      record_error(status, KERR_TIMEOUT);
+      break;
+    }
+  }
+  __threadfence_system();
+}
+
+}  // namespace
+
+cudaError_t launch_gather_wait(unsigned* cnt, unsigned* expected, unsigned signals,
+                               unsigned* status, cudaStream_t st) {
+  gather_wait_kernel<<<1, 32, 0, st>>>(cnt, expected, signals, status);
+  return cudaGetLastError();
+}
+
+}  // namespace vtq

@@ -74,6 +74,7 @@ struct KqParams {
   int x_smem;               // x rows fetched by TMA into off_xf
   uint32_t off_xd, off_bsum, off_xq, off_xf, off_stage;
   unsigned* status;
+  GatherTarget g;           // g.world > 0: fused all-gather of y to every rank
 };
 
 // quantize_block_q8 for every (batch row, superblock): one warp per block,
@@ -353,7 +354,18 @@ __device__ __forceinline__ void consume_pass(const KqParams& p, const uint8_t* s
 #pragma unroll
       for (int c = 0; c < NCH; c++) v[c] = part[c][b];
       const float t = seg_fixed_tree<NCH>(v, sl, p.lpr, p.S);
-      if (row_ok && sl == 0) p.y[(int64_t)b * p.ldy + yrow] = t;
+      if (row_ok && sl == 0) {
+        if (p.g.world == 0) {
+          p.y[(int64_t)b * p.ldy + yrow] = t;
+        } else {
+          // Row-sharded linear: store this row into every rank's full y
+          // (peer memory over NVLink for q != this rank).
+          const int64_t at = (int64_t)b * p.g.ldy + p.g.row0 + yrow;
+#pragma unroll
+          for (int q = 0; q < kMaxRanks; q++)
+            if (q < p.g.world) p.g.y[q][at] = t;
+        }
+      }
     }
   }
 }
@@ -493,6 +505,23 @@ __global__ void __launch_bounds__((CW + 1) * 32, VTQ_KQ_CTAS) kq_matvec_kernel(c
     }
   }
   if (tid == 0) KQ_TRACE(5);
+  if (p.g.world > 0) {
+    // Publish: every storing thread fences at system scope, then the last CTA
+    // of the launch (completion counter in this rank's memory) signals every
+    // rank's arrival counter once.
+    __threadfence_system();
+    asm volatile("bar.sync 1, %0;" ::"n"(CW * 32));
+    if (tid == 0) {
+      const unsigned prev = atomicAdd(p.g.done, 1u);
+      if (prev == gridDim.x - 1) {
+        *p.g.done = 0;  // every CTA of this launch has counted
+        __threadfence_system();
+#pragma unroll
+        for (int q = 0; q < kMaxRanks; q++)
+          if (q < p.g.world) atomicAdd_system(p.g.cnt[q], 1u);
+      }
+    }
+  }
 }
 
 bool use_pdl() {
@@ -568,7 +597,8 @@ int max_smem_optin() {
 static inline uint32_t align_up(uint32_t v, uint32_t a) { return (v + a - 1) / a * a; }
 
 cudaError_t launch_kq_matvec(const DevMatrix& m, const float* x, int64_t ldx, int64_t batch,
-                             float* y, int64_t ldy, unsigned* status, cudaStream_t st) {
+                             float* y, int64_t ldy, unsigned* status, cudaStream_t st,
+                             const GatherTarget* g) {
   constexpr int KQ_BMAX = 4;  // activation rows per launch
   if (m.dtype != T_Q4_K && m.dtype != T_Q6_K) return cudaErrorInvalidValue;
   const int S = (int)(m.in_feat / 256);
@@ -603,6 +633,10 @@ cudaError_t launch_kq_matvec(const DevMatrix& m, const float* x, int64_t ldx, in
     p.y = y + b0 * ldy;
     p.ldy = ldy;
     p.status = status;
+    if (g) {
+      if (g->world < 1 || g->world > kMaxRanks || batch > KQ_BMAX) return cudaErrorInvalidValue;
+      p.g = *g;
+    }
     p.lpr = lpr;
     const int NB = m.dtype == T_Q4_K ? BsumStride<8>::v : BsumStride<16>::v;
     constexpr uint32_t kBarBytes = (2 * KQ_NST_MAX + 1) * 8;  // full[], empty[], xbar

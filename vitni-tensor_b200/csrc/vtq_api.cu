@@ -406,3 +406,114 @@ vtq_status vtq_linear_device(int32_t dtype, const uint8_t* w_dev, int64_t in_fea
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Row-sharded linears with the all-gather fused into the kernel (NVLink P2P).
+
+struct vtq_gather {
+  int device = 0, world = 0, rank = 0;
+  uint8_t* base = nullptr;                    // [counters 256 B | y]
+  uint8_t* peer[kMaxRanks] = {};              // every rank's base (own included)
+  size_t y_floats = 0;
+};
+
+namespace {
+constexpr size_t kGatherHdr = 256;  // cnt @0, expected @4, done @8
+}
+
+vtq_status vtq_gather_create(vtq_ctx* c, int32_t world, int32_t rank, size_t y_floats,
+                             vtq_gather** out, uint8_t* ipc_handle) {
+  if (!c || !out || !ipc_handle) return fail(c, VTQ_ERR_INVALID_ARG, "null argument");
+  if (world < 1 || world > kMaxRanks || rank < 0 || rank >= world || y_floats == 0)
+    return fail(c, VTQ_ERR_INVALID_ARG, "vtq_gather_create: bad world / rank / size");
+  VTQ_CUDA(c, cudaSetDevice(c->device));
+  auto* g = new vtq_gather;
+  g->device = c->device;
+  g->world = world;
+  g->rank = rank;
+  g->y_floats = y_floats;
+  cudaError_t e = cudaMalloc(&g->base, kGatherHdr + y_floats * 4);
+  if (e == cudaSuccess) e = cudaMemset(g->base, 0, kGatherHdr + y_floats * 4);
+  cudaIpcMemHandle_t h;
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, g->base);
+  if (e != cudaSuccess) {
+    if (g->base) cudaFree(g->base);
+    delete g;
+    return fail(c, VTQ_ERR_GPU, std::string("vtq_gather_create: ") + cudaGetErrorString(e));
+  }
+  static_assert(sizeof(h) == 64, "IPC handle size");
+  memcpy(ipc_handle, &h, 64);
+  g->peer[rank] = g->base;
+  *out = g;
+  return VTQ_OK;
+}
+
+vtq_status vtq_gather_connect(vtq_gather* g, const uint8_t* handles) {
+  if (!g || !handles) return VTQ_ERR_INVALID_ARG;
+  if (cudaSetDevice(g->device) != cudaSuccess) return VTQ_ERR_GPU;
+  for (int q = 0; q < g->world; q++) {
+    if (q == g->rank || g->peer[q]) continue;
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handles + 64 * q, 64);
+    void* p = nullptr;
+    if (cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess)
+      return VTQ_ERR_GPU;
+    g->peer[q] = static_cast<uint8_t*>(p);
+  }
+  return VTQ_OK;
+}
+
+float* vtq_gather_y(vtq_gather* g) {
+  return g ? reinterpret_cast<float*>(g->base + kGatherHdr) : nullptr;
+}
+
+vtq_status vtq_linear_gather(vtq_ctx* c, const vtq_weight* w, const float* x, int64_t batch,
+                             vtq_gather* g, int64_t y_offset, int64_t ldy, int64_t row0,
+                             uint32_t flags) {
+  if (!c || !w || !x || !g) return fail(c, VTQ_ERR_INVALID_ARG, "null argument");
+  for (int q = 0; q < g->world; q++)
+    if (!g->peer[q]) return fail(c, VTQ_ERR_INVALID_ARG, "vtq_linear_gather: gather not connected");
+  const DevMatrix& m = w->m;
+  if (!(m.dtype == T_Q6_K || (m.dtype == T_Q4_K && !(flags & VTQ_Q4K_FLOAT))))
+    return fail(c, VTQ_ERR_NOT_IMPLEMENTED,
+                "vtq_linear_gather: not implemented (fused gather needs an integer k-quant weight)");
+  if (batch < 1 || batch > 4)
+    return fail(c, VTQ_ERR_NOT_IMPLEMENTED, "vtq_linear_gather: batch must be 1..4");
+  if (row0 < 0 || row0 + m.out_feat > ldy || y_offset < 0 ||
+      (size_t)(y_offset + batch * ldy) > g->y_floats)
+    return fail(c, VTQ_ERR_INVALID_ARG, "vtq_linear_gather: rows outside the gather buffer");
+  if (vtq_status s = check_kernel_limits(c, m, flags)) return s;
+  VTQ_CUDA(c, cudaSetDevice(c->device));
+  GatherTarget t{};
+  t.world = g->world;
+  t.row0 = row0;
+  t.ldy = ldy;
+  for (int q = 0; q < g->world; q++) {
+    t.y[q] = reinterpret_cast<float*>(g->peer[q] + kGatherHdr) + y_offset;
+    t.cnt[q] = reinterpret_cast<unsigned*>(g->peer[q]);
+  }
+  t.done = reinterpret_cast<unsigned*>(g->base + 8);
+  VTQ_CUDA(c, launch_kq_matvec(m, x, m.in_feat, batch, nullptr, 0,
+                               reinterpret_cast<unsigned*>(c->io), c->stream, &t));
+  return VTQ_OK;
+}
+
+vtq_status vtq_gather_wait(vtq_ctx* c, vtq_gather* g, uint32_t signals) {
+  if (!c || !g) return VTQ_ERR_INVALID_ARG;
+  VTQ_CUDA(c, cudaSetDevice(c->device));
+  VTQ_CUDA(c, launch_gather_wait(reinterpret_cast<unsigned*>(g->base),
+                                 reinterpret_cast<unsigned*>(g->base + 4), signals,
+                                 reinterpret_cast<unsigned*>(c->io), c->stream));
+  return VTQ_OK;
+}
+
+vtq_status vtq_gather_destroy(vtq_gather* g) {
+  if (!g) return VTQ_OK;
+  cudaSetDevice(g->device);
+  cudaDeviceSynchronize();
+  for (int q = 0; q < g->world; q++)
+    if (q != g->rank && g->peer[q]) cudaIpcCloseMemHandle(g->peer[q]);
+  cudaFree(g->base);
+  delete g;
+  return VTQ_OK;
+}

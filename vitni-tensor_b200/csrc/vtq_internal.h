@@ -30,10 +30,33 @@ int64_t device_pitch(int dtype, int64_t in_feat);
 cudaError_t launch_repack(const uint8_t* staging, const DevMatrix& m, uint8_t* dst,
                           cudaStream_t st);
 
+// Fused all-gather target of a row-sharded linear: the kernel stores its rows
+// into the full-y buffer of every rank (peer pointers over NVLink, rows
+// [row0, row0 + R) of a [batch][ldy] array at y[q]) and, once every CTA of
+// the launch has stored, adds 1 to every rank's arrival counter cnt[q].
+// `done` is a launch-completion counter in this rank's memory (starts at 0,
+// left at 0).
+constexpr int kMaxRanks = 8;
+struct GatherTarget {
+  int world;
+  int64_t row0, ldy;
+  float* y[kMaxRanks];
+  unsigned* cnt[kMaxRanks];
+  unsigned* done;
+};
+
 // Integer k-quant matvec (Q4_K / Q6_K against int8-quantised activations):
 // y[b, r] for r in [0, R), b in [0, batch). x row stride ldx, y row stride ldy.
+// With `g`, y/ldy are ignored and the rows go to every rank of g instead.
 cudaError_t launch_kq_matvec(const DevMatrix& m, const float* x, int64_t ldx, int64_t batch,
-                             float* y, int64_t ldy, unsigned* status, cudaStream_t st);
+                             float* y, int64_t ldy, unsigned* status, cudaStream_t st,
+                             const GatherTarget* g = nullptr);
+
+// Waits on `st` until this rank's arrival counter has received `signals` more
+// arrivals than before (`expected` is a device counter of arrivals consumed).
+// Bounded: after 2 s the status word gets KERR_TIMEOUT.
+cudaError_t launch_gather_wait(unsigned* cnt, unsigned* expected, unsigned signals,
+                               unsigned* status, cudaStream_t st);
 
 // Batched integer Q4_K linear on the tensor cores (tcgen05 kind::i8): same
 // results as launch_kq_matvec for any batch; used for prefill-sized batches.

@@ -38,6 +38,8 @@ EXPORTS = (
     "vtq_device_repack", "vtq_linear_device", "vtq_decode_open", "vtq_decode_last_error",
     "vtq_decode_config", "vtq_decode_run", "vtq_decode_close", "vtq_expf", "vtq_sinf",
     "vtq_cosf", "vtq_powf", "vtq_libm_sweep", "vtq_linear_host_noalloc",
+    "vtq_gather_create", "vtq_gather_connect", "vtq_gather_y", "vtq_linear_gather",
+    "vtq_gather_wait", "vtq_gather_destroy",
     "vtq_decode_timing", "vtq_decode_debug_buffer",
 )
 
@@ -130,6 +132,12 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         "vtq_decode_timing": (c_i32, [c_p, c_p]),
         "vtq_decode_debug_buffer": (c_i32, [c_p, ctypes.c_int, c_p, c_sz]),
         "vtq_linear_host_noalloc": (c_i32, [c_i32, c_p, c_i64, c_i64, c_p, c_p, c_i64, c_p]),
+        "vtq_gather_create": (c_i32, [c_p, c_i32, c_i32, c_sz, ctypes.POINTER(c_p), c_p]),
+        "vtq_gather_connect": (c_i32, [c_p, c_p]),
+        "vtq_gather_y": (c_p, [c_p]),
+        "vtq_linear_gather": (c_i32, [c_p, c_p, c_p, c_i64, c_p, c_i64, c_i64, c_i64, c_u32]),
+        "vtq_gather_wait": (c_i32, [c_p, c_p, c_u32]),
+        "vtq_gather_destroy": (c_i32, [c_p]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -275,6 +283,45 @@ def linear_dispatch(ctx: Context, x, w: QuantTensor, in_feat: int, out_feat: int
                                            in_feat, out_feat, _ptr(y),
                                            Q4K_FLOAT if q4k_float else 0))
     return y
+
+
+class Gather:
+    """Fused row-shard all-gather over NVLink (one per rank of a process group).
+
+    Every rank owns a full-y buffer of `y_floats` floats; `linear` computes this
+    rank's rows of a row-sharded weight and stores them into every rank's
+    buffer, `wait` holds the stream until the expected ranks have arrived.
+    The buffer handles are exchanged with torch.distributed (all_gather_object).
+    """
+
+    def __init__(self, ctx: "Context", y_floats: int, group=None):
+        import torch.distributed as dist
+        self.ctx, self.lib = ctx, ctx.lib
+        self.world, self.rank = dist.get_world_size(group), dist.get_rank(group)
+        h = ctypes.c_void_p()
+        ipc = ctypes.create_string_buffer(64)
+        ctx._check(self.lib.vtq_gather_create(ctx.handle, self.world, self.rank, y_floats,
+                                              ctypes.byref(h), ipc))
+        self.handle = h
+        handles = [None] * self.world
+        dist.all_gather_object(handles, ipc.raw, group=group)
+        blob = b"".join(handles)
+        ctx._check(self.lib.vtq_gather_connect(self.handle, blob))
+        self.y_ptr = self.lib.vtq_gather_y(self.handle)
+        self.y_floats = y_floats
+
+    def linear(self, w: "Weight", x_ptr: int, row0: int, ldy: int, y_offset: int = 0,
+               batch: int = 1):
+        self.ctx._check(self.lib.vtq_linear_gather(self.ctx.handle, w.handle, x_ptr, batch,
+                                                   self.handle, y_offset, ldy, row0, 0))
+
+    def wait(self, signals: int):
+        self.ctx._check(self.lib.vtq_gather_wait(self.ctx.handle, self.handle, signals))
+
+    def close(self):
+        if self.handle:
+            self.lib.vtq_gather_destroy(self.handle)
+            self.handle = None
 
 
 class DecodeSession:
