@@ -38,6 +38,30 @@ cudaError_t launch_kq_or_canon(const DevMatrix& m, const float* x, float* y, uns
 
 namespace {
 
+// Programmatic dependent launch: every kernel of a step waits for its
+// predecessor before touching data, then lets its own successor start (the
+// next matvec streams its weights while this kernel runs).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_release() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), unsigned grid, unsigned block, size_t smem,
+                       cudaStream_t st, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(block);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 // ---------------------------------------------------------------- GGUF ----
 // Zero-copy parse of a GGUF v2/v3 blob (src/model/gguf.rs:305-422): metadata
 // scalars and strings, tensor infos, alignment, tensor byte ranges.
@@ -246,10 +270,12 @@ __global__ void embed_kernel(const uint8_t* table, int dtype, int64_t pitch, int
 
 // x = x + delta (if delta), then xb = rms_norm(x) * w (rms_norm.rs:94-108):
 // sumsq accumulated serially in element order by one thread.
-__global__ void rmsnorm_kernel(float* x, const float* delta, const float* w, float eps, int n,
+__global__ void __launch_bounds__(256) rmsnorm_kernel(float* x, const float* delta, const float* w, float eps, int n,
                                float* out) {
   extern __shared__ float sq[];
   __shared__ float s_scale;
+  pdl_wait();
+  pdl_release();
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
     float v = x[i];
     if (delta) {
@@ -260,14 +286,32 @@ __global__ void rmsnorm_kernel(float* x, const float* delta, const float* w, flo
   }
   __syncthreads();
   if (threadIdx.x == 0) {
+    // The reference's serial sum (rms_norm.rs:97-100): one dependent fp32 add
+    // per element. Loads run a batch ahead so the chain is add latency only.
     float s = 0.0f;
-    for (int i = 0; i < n; i += 4) {
-      const float4 q = *reinterpret_cast<const float4*>(sq + i);
-      s = __fadd_rn(s, q.x);
-      if (i + 1 < n) s = __fadd_rn(s, q.y);
-      if (i + 2 < n) s = __fadd_rn(s, q.z);
-      if (i + 3 < n) s = __fadd_rn(s, q.w);
+    const float4* q4 = reinterpret_cast<const float4*>(sq);
+    const int n4 = n / 4, nb = n4 / 8;
+    float4 a[8], b[8];
+    if (nb > 0) {
+#pragma unroll
+      for (int u = 0; u < 8; u++) a[u] = q4[u];
     }
+    for (int c = 0; c < nb; c++) {
+      if (c + 1 < nb) {
+#pragma unroll
+        for (int u = 0; u < 8; u++) b[u] = q4[8 * (c + 1) + u];
+      }
+#pragma unroll
+      for (int u = 0; u < 8; u++) {
+        s = __fadd_rn(s, a[u].x);
+        s = __fadd_rn(s, a[u].y);
+        s = __fadd_rn(s, a[u].z);
+        s = __fadd_rn(s, a[u].w);
+      }
+#pragma unroll
+      for (int u = 0; u < 8; u++) a[u] = b[u];
+    }
+    for (int i = 32 * nb; i < n; i++) s = __fadd_rn(s, sq[i]);
     const float mean = __fdiv_rn(s, (float)n);
     s_scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
   }
@@ -279,50 +323,72 @@ __global__ void rmsnorm_kernel(float* x, const float* delta, const float* w, flo
   }
 }
 
-// Cache v and k at pos, then interleaved RoPE on q and the cached k
-// (forward_quantized.rs:407-472). rope tables: [seq_len][head_size / 2].
-__global__ void rope_kv_kernel(float* q, const float* k, const float* v, float* kc, float* vc,
-                               int layer, int seq_len, int dim, int kv_dim, int hs,
-                               const float* rcos, const float* rsin, const StepState* st) {
-  const int pos = st->pos;
+// Attention for one query head with the step's RoPE fused in
+// (forward_quantized.rs:407-500): rotate this head's q and its kv head's new
+// k (interleaved pairs, host cos/sin tables), store the rotated k and the raw
+// v at `pos` of the cache (first query head of each kv group), then serial
+// scores over head_dim, softmax with a serial sum, and a serial P.V sum over
+// positions for every head dimension. Positions < pos come from the cache;
+// position pos uses the k/v computed here (the same values the cache gets).
+__global__ void attention_rope_kernel(const float* q, const float* k, const float* v, float* kc,
+                                      float* vc, int layer, int seq_len, int kv_dim, int hs,
+                                      int kv_mul, const float* rcos, const float* rsin,
+                                      const StepState* st, float* out) {
+  extern __shared__ float sm[];
+  float* qh = sm;            // [hs] rotated query head
+  float* kh = sm + hs;       // [hs] rotated new key
+  float* vh = sm + 2 * hs;   // [hs] new value
+  float* att = sm + 3 * hs;  // [pos + 1]
+  __shared__ float s_max, s_inv;
+  pdl_wait();
+  pdl_release();
+  const int h = blockIdx.x, g = h / kv_mul, pos = st->pos, np = pos + 1;
   const size_t off = ((size_t)layer * seq_len + pos) * kv_dim;
-  for (int p = blockIdx.x * blockDim.x + threadIdx.x; p < dim / 2;
-       p += gridDim.x * blockDim.x) {
-    const int i = 2 * p;
-    const int idx = i % hs;
-    const float fcr = rcos[(size_t)pos * (hs / 2) + idx / 2];
-    const float fci = rsin[(size_t)pos * (hs / 2) + idx / 2];
-    const float q0 = q[i], q1 = q[i + 1];
-    q[i] = __fsub_rn(__fmul_rn(q0, fcr), __fmul_rn(q1, fci));
-    q[i + 1] = __fadd_rn(__fmul_rn(q0, fci), __fmul_rn(q1, fcr));
-    if (i < kv_dim) {
-      const float k0 = k[i], k1 = k[i + 1];
-      kc[off + i] = __fsub_rn(__fmul_rn(k0, fcr), __fmul_rn(k1, fci));
-      kc[off + i + 1] = __fadd_rn(__fmul_rn(k0, fci), __fmul_rn(k1, fcr));
-      vc[off + i] = v[i];
-      vc[off + i + 1] = v[i + 1];
+  for (int p = threadIdx.x; p < hs / 2; p += blockDim.x) {
+    const float fcr = rcos[(size_t)pos * (hs / 2) + p], fci = rsin[(size_t)pos * (hs / 2) + p];
+    const float q0 = q[h * hs + 2 * p], q1 = q[h * hs + 2 * p + 1];
+    qh[2 * p] = __fsub_rn(__fmul_rn(q0, fcr), __fmul_rn(q1, fci));
+    qh[2 * p + 1] = __fadd_rn(__fmul_rn(q0, fci), __fmul_rn(q1, fcr));
+    const float k0 = k[g * hs + 2 * p], k1 = k[g * hs + 2 * p + 1];
+    const float r0 = __fsub_rn(__fmul_rn(k0, fcr), __fmul_rn(k1, fci));
+    const float r1 = __fadd_rn(__fmul_rn(k0, fci), __fmul_rn(k1, fcr));
+    kh[2 * p] = r0;
+    kh[2 * p + 1] = r1;
+    vh[2 * p] = v[g * hs + 2 * p];
+    vh[2 * p + 1] = v[g * hs + 2 * p + 1];
+    if (h % kv_mul == 0) {
+      kc[off + g * hs + 2 * p] = r0;
+      kc[off + g * hs + 2 * p + 1] = r1;
+      vc[off + g * hs + 2 * p] = vh[2 * p];
+      vc[off + g * hs + 2 * p + 1] = vh[2 * p + 1];
     }
   }
-}
-
-// One CTA per head (forward_quantized.rs:476-500, softmax :925-941).
-__global__ void attention_kernel(const float* q, const float* kc, const float* vc, int layer,
-                                 int seq_len, int kv_dim, int hs, int kv_mul, const StepState* st,
-                                 float* out) {
-  extern __shared__ float sm[];
-  float* qh = sm;        // [hs]
-  float* att = sm + hs;  // [pos + 1]
-  __shared__ float s_max, s_inv;
-  const int h = blockIdx.x, pos = st->pos, np = pos + 1;
-  const float* kbase = kc + (size_t)layer * seq_len * kv_dim + (h / kv_mul) * hs;
-  const float* vbase = vc + (size_t)layer * seq_len * kv_dim + (h / kv_mul) * hs;
-  for (int d = threadIdx.x; d < hs; d += blockDim.x) qh[d] = q[h * hs + d];
   __syncthreads();
+  const float* kbase = kc + (size_t)layer * seq_len * kv_dim + g * hs;
+  const float* vbase = vc + (size_t)layer * seq_len * kv_dim + g * hs;
   const float root = __fsqrt_rn((float)hs);
   for (int t = threadIdx.x; t < np; t += blockDim.x) {
-    const float* kt = kbase + (size_t)t * kv_dim;
+    const float* kt = (t == pos) ? kh : kbase + (size_t)t * kv_dim;
     float score = 0.0f;
-    for (int d = 0; d < hs; d++) score = __fadd_rn(score, __fmul_rn(qh[d], kt[d]));
+    if ((hs & 15) == 0) {
+      for (int d0 = 0; d0 < hs; d0 += 16) {
+        float4 kv4[4], qv4[4];
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+          kv4[u] = *reinterpret_cast<const float4*>(kt + d0 + 4 * u);
+          qv4[u] = *reinterpret_cast<const float4*>(qh + d0 + 4 * u);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+          score = __fadd_rn(score, __fmul_rn(qv4[u].x, kv4[u].x));
+          score = __fadd_rn(score, __fmul_rn(qv4[u].y, kv4[u].y));
+          score = __fadd_rn(score, __fmul_rn(qv4[u].z, kv4[u].z));
+          score = __fadd_rn(score, __fmul_rn(qv4[u].w, kv4[u].w));
+        }
+      }
+    } else {
+      for (int d = 0; d < hs; d++) score = __fadd_rn(score, __fmul_rn(qh[d], kt[d]));
+    }
     att[t] = __fdiv_rn(score, root);
   }
   __syncthreads();
@@ -337,7 +403,15 @@ __global__ void attention_kernel(const float* q, const float* kc, const float* v
   __syncthreads();
   if (threadIdx.x == 0) {
     float sum = 0.0f;
-    for (int t = 0; t < np; t++) sum = __fadd_rn(sum, att[t]);
+    int t = 0;
+    for (; t + 4 <= np; t += 4) {
+      const float a0 = att[t], a1 = att[t + 1], a2 = att[t + 2], a3 = att[t + 3];
+      sum = __fadd_rn(sum, a0);
+      sum = __fadd_rn(sum, a1);
+      sum = __fadd_rn(sum, a2);
+      sum = __fadd_rn(sum, a3);
+    }
+    for (; t < np; t++) sum = __fadd_rn(sum, att[t]);
     s_inv = __fdiv_rn(1.0f, sum);
   }
   __syncthreads();
@@ -345,14 +419,25 @@ __global__ void attention_kernel(const float* q, const float* kc, const float* v
   __syncthreads();
   for (int d = threadIdx.x; d < hs; d += blockDim.x) {
     float acc = 0.0f;
-    for (int t = 0; t < np; t++)
-      acc = __fadd_rn(acc, __fmul_rn(att[t], vbase[(size_t)t * kv_dim + d]));
+    int t = 0;
+    for (; t + 4 <= pos; t += 4) {
+      const float v0 = vbase[(size_t)t * kv_dim + d], v1 = vbase[(size_t)(t + 1) * kv_dim + d];
+      const float v2 = vbase[(size_t)(t + 2) * kv_dim + d], v3 = vbase[(size_t)(t + 3) * kv_dim + d];
+      acc = __fadd_rn(acc, __fmul_rn(att[t], v0));
+      acc = __fadd_rn(acc, __fmul_rn(att[t + 1], v1));
+      acc = __fadd_rn(acc, __fmul_rn(att[t + 2], v2));
+      acc = __fadd_rn(acc, __fmul_rn(att[t + 3], v3));
+    }
+    for (; t < pos; t++) acc = __fadd_rn(acc, __fmul_rn(att[t], vbase[(size_t)t * kv_dim + d]));
+    acc = __fadd_rn(acc, __fmul_rn(att[pos], vh[d]));
     out[h * hs + d] = acc;
   }
 }
 
 // SwiGLU: silu(g) * up with silu = g / (1 + expf(-g)) (forward_quantized.rs:556-561).
 __global__ void swiglu_kernel(const float* g, const float* u, float* out, int n) {
+  pdl_wait();
+  pdl_release();
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
     const float gi = g[i];
     const float silu = __fdiv_rn(gi, __fadd_rn(1.0f, libm::expf(-gi)));
@@ -366,6 +451,8 @@ __global__ void argmax_next_kernel(const float* logits, int n, StepState* st,
                                    const uint32_t* prompt, uint32_t* out_tokens) {
   __shared__ float bv[32];
   __shared__ int bi[32];
+  pdl_wait();
+  pdl_release();
   float best = -INFINITY;
   int besti = 0x7fffffff;
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
@@ -409,6 +496,8 @@ __global__ void argmax_next_kernel(const float* logits, int n, StepState* st,
 // Copy the step's logits into the per-position log (optional output).
 __global__ void log_logits_kernel(const float* logits, int vocab, const StepState* st,
                                   float* log) {
+  pdl_wait();
+  pdl_release();
   const int pos = st->pos;
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < vocab; i += gridDim.x * blockDim.x)
     log[(size_t)pos * vocab + i] = logits[i];
@@ -430,6 +519,10 @@ struct vtq_decode {
   struct Layer {
     float *rms_att, *rms_ffn;
     DevMatrix wq, wk, wv, wo, w1, w2, w3;
+    // q|k and gate|up share their input: when each pair has one dtype, the two
+    // matrices sit back to back in HBM and run as one launch (wqk, w13).
+    bool fused_qk = false, fused_13 = false;
+    DevMatrix wqk{}, w13{};
   };
   std::vector<Layer> layers;
   float* rms_final = nullptr;
@@ -472,7 +565,8 @@ vtq_status dalloc(vtq_decode* d, T** p, size_t bytes) {
   return VTQ_OK;
 }
 
-vtq_status upload_matrix(vtq_decode* d, const GTensor& t, int64_t in, int64_t out, DevMatrix* m) {
+vtq_status upload_matrix(vtq_decode* d, const GTensor& t, int64_t in, int64_t out, DevMatrix* m,
+                         uint8_t* into = nullptr) {
   if (t.shape.size() != 2 || (int64_t)t.shape[0] != in || (int64_t)t.shape[1] != out)
     return dfail(d, VTQ_ERR_INTERNAL, "gguf: weight shape mismatch");
   const int64_t rb = packed_row_bytes(t.dtype, in);
@@ -482,8 +576,9 @@ vtq_status upload_matrix(vtq_decode* d, const GTensor& t, int64_t in, int64_t ou
   m->out_feat = out;
   m->row_bytes = rb;
   m->pitch = device_pitch(t.dtype, in);
-  uint8_t *dst, *stage;
-  if (vtq_status s = dalloc(d, &dst, (size_t)(out * m->pitch + 16))) return s;
+  uint8_t *dst = into, *stage;
+  if (!dst)
+    if (vtq_status s = dalloc(d, &dst, (size_t)(out * m->pitch + 16))) return s;
   DCUDA(d, cudaMalloc(&stage, t.len));
   DCUDA(d, cudaMemcpyAsync(stage, t.bytes, t.len, cudaMemcpyHostToDevice, d->stream));
   DCUDA(d, launch_repack(stage, *m, dst, d->stream));
@@ -542,32 +637,44 @@ vtq_status enqueue_step(vtq_decode* d, bool log_logits) {
   embed_kernel<<<(dim + 255) / 256, 256, 0, s>>>(d->embd.data, d->embd.dtype, d->embd.pitch, dim,
                                                   d->st, d->x);
   const size_t rms_smem = ((size_t)dim + 4) * 4;
+  const size_t att_smem = ((size_t)3 * hs + d->seq_len) * 4;
   const float* delta = nullptr;
   for (int l = 0; l < d->n_layers; l++) {
     auto& L = d->layers[l];
-    rmsnorm_kernel<<<1, 1024, rms_smem, s>>>(d->x, delta, L.rms_att, d->rms_eps, dim, d->xb);
-    DCUDA(d, launch_kq_or_canon(L.wq, d->xb, d->q, d->status, s));
-    DCUDA(d, launch_kq_or_canon(L.wk, d->xb, d->k, d->status, s));
+    DCUDA(d, launch_pdl(rmsnorm_kernel, 1, 256, rms_smem, s, d->x, delta, L.rms_att,
+                        d->rms_eps, dim, d->xb));
+    if (L.fused_qk) {
+      DCUDA(d, launch_kq_or_canon(L.wqk, d->xb, d->q, d->status, s));
+    } else {
+      DCUDA(d, launch_kq_or_canon(L.wq, d->xb, d->q, d->status, s));
+      DCUDA(d, launch_kq_or_canon(L.wk, d->xb, d->k, d->status, s));
+    }
     DCUDA(d, launch_kq_or_canon(L.wv, d->xb, d->v, d->status, s));
-    rope_kv_kernel<<<(dim / 2 + 255) / 256, 256, 0, s>>>(d->q, d->k, d->v, d->kc, d->vc, l,
-                                                        d->seq_len, dim, kv_dim, hs, d->rcos,
-                                                        d->rsin, d->st);
-    attention_kernel<<<d->n_heads, 128, ((size_t)hs + d->seq_len) * 4, s>>>(
-        d->q, d->kc, d->vc, l, d->seq_len, kv_dim, hs, kv_mul, d->st, d->xo);
+    DCUDA(d, launch_pdl(attention_rope_kernel, d->n_heads, 128, att_smem, s, d->q, d->k, d->v,
+                        d->kc, d->vc, l, d->seq_len, kv_dim, hs, kv_mul, d->rcos, d->rsin, d->st,
+                        d->xo));
     DCUDA(d, launch_kq_or_canon(L.wo, d->xo, d->xb2, d->status, s));
-    rmsnorm_kernel<<<1, 1024, rms_smem, s>>>(d->x, d->xb2, L.rms_ffn, d->rms_eps, dim, d->xb);
-    DCUDA(d, launch_kq_or_canon(L.w1, d->xb, d->g, d->status, s));
-    DCUDA(d, launch_kq_or_canon(L.w3, d->xb, d->u, d->status, s));
-    swiglu_kernel<<<(d->hidden + 255) / 256, 256, 0, s>>>(d->g, d->u, d->inner, d->hidden);
+    DCUDA(d, launch_pdl(rmsnorm_kernel, 1, 256, rms_smem, s, d->x, d->xb2, L.rms_ffn,
+                        d->rms_eps, dim, d->xb));
+    if (L.fused_13) {
+      DCUDA(d, launch_kq_or_canon(L.w13, d->xb, d->g, d->status, s));
+    } else {
+      DCUDA(d, launch_kq_or_canon(L.w1, d->xb, d->g, d->status, s));
+      DCUDA(d, launch_kq_or_canon(L.w3, d->xb, d->u, d->status, s));
+    }
+    DCUDA(d, launch_pdl(swiglu_kernel, (d->hidden + 255) / 256, 256, 0, s, d->g, d->u, d->inner,
+                        d->hidden));
     DCUDA(d, launch_kq_or_canon(L.w2, d->inner, d->xb2, d->status, s));
     delta = d->xb2;
   }
-  rmsnorm_kernel<<<1, 1024, rms_smem, s>>>(d->x, delta, d->rms_final, d->rms_eps, dim, d->xb);
+  DCUDA(d, launch_pdl(rmsnorm_kernel, 1, 256, rms_smem, s, d->x, delta, d->rms_final,
+                      d->rms_eps, dim, d->xb));
   DCUDA(d, launch_kq_or_canon(d->head, d->xb, d->logits, d->status, s));
   if (log_logits)
-    log_logits_kernel<<<(d->vocab + 255) / 256, 256, 0, s>>>(d->logits, d->vocab, d->st,
-                                                              d->logit_log);
-  argmax_next_kernel<<<1, 1024, 0, s>>>(d->logits, d->vocab, d->st, d->prompt, d->out_tokens);
+    DCUDA(d, launch_pdl(log_logits_kernel, (d->vocab + 255) / 256, 256, 0, s, d->logits,
+                        d->vocab, d->st, d->logit_log));
+  DCUDA(d, launch_pdl(argmax_next_kernel, 1, 1024, 0, s, d->logits, d->vocab, d->st, d->prompt,
+                      d->out_tokens));
   DCUDA(d, cudaGetLastError());
   return VTQ_OK;
 }
@@ -657,7 +764,31 @@ vtq_status vtq_decode_open(vtq_ctx* ctx, int device, const uint8_t* gguf, size_t
                 {"attn_v.weight", dim, kv_dim, &L.wv},      {"attn_output.weight", dim, dim, &L.wo},
                 {"ffn_gate.weight", dim, d->hidden, &L.w1}, {"ffn_down.weight", d->hidden, dim, &L.w2},
                 {"ffn_up.weight", dim, d->hidden, &L.w3}};
+    const GTensor* tq = need(d, g, p + "attn_q.weight");
+    const GTensor* tk = need(d, g, p + "attn_k.weight");
+    const GTensor* t1 = need(d, g, p + "ffn_gate.weight");
+    const GTensor* t3 = need(d, g, p + "ffn_up.weight");
+    if (!tq || !tk || !t1 || !t3) return VTQ_ERR_INTERNAL;
+    auto fuse = [&](const GTensor* ta, const GTensor* tb, int64_t in, int64_t ra, int64_t rb,
+                    DevMatrix* ma, DevMatrix* mb, DevMatrix* both, bool* fused) -> vtq_status {
+      if (ta->dtype != tb->dtype || (ta->dtype != T_Q4_K && ta->dtype != T_Q6_K)) return VTQ_OK;
+      const int64_t pitch = device_pitch(ta->dtype, in);
+      if (pitch <= 0) return VTQ_OK;
+      uint8_t* buf;
+      if (vtq_status e = dalloc(d, &buf, (size_t)((ra + rb) * pitch + 16))) return e;
+      if (vtq_status e = upload_matrix(d, *ta, in, ra, ma, buf)) return e;
+      if (vtq_status e = upload_matrix(d, *tb, in, rb, mb, buf + ra * pitch)) return e;
+      *both = *ma;
+      both->out_feat = ra + rb;
+      *fused = true;
+      return VTQ_OK;
+    };
+    if ((s = fuse(tq, tk, dim, dim, kv_dim, &L.wq, &L.wk, &L.wqk, &L.fused_qk))) return s;
+    if ((s = fuse(t1, t3, dim, d->hidden, d->hidden, &L.w1, &L.w3, &L.w13, &L.fused_13))) return s;
     for (auto& mm : mats) {
+      if ((L.fused_qk && (mm.m == &L.wq || mm.m == &L.wk)) ||
+          (L.fused_13 && (mm.m == &L.w1 || mm.m == &L.w3)))
+        continue;
       const GTensor* t = need(d, g, p + mm.name);
       if (!t) return VTQ_ERR_INTERNAL;
       if ((s = upload_matrix(d, *t, mm.in, mm.out, mm.m))) return s;
@@ -686,12 +817,15 @@ vtq_status vtq_decode_open(vtq_ctx* ctx, int device, const uint8_t* gguf, size_t
   // before the first decode step.
   DCUDA(d, cudaMemsetAsync(d->kc, 0, kvb, d->stream));
   DCUDA(d, cudaMemsetAsync(d->vc, 0, kvb, d->stream));
-  float** bufs[] = {&d->x, &d->xb, &d->q, &d->xo, &d->xb2};
+  float** bufs[] = {&d->x, &d->xb, &d->xo, &d->xb2};
   for (float** b : bufs)
     if ((s = dalloc(d, b, (size_t)dim * 4))) return s;
-  if ((s = dalloc(d, &d->k, (size_t)kv_dim * 4)) || (s = dalloc(d, &d->v, (size_t)kv_dim * 4)) ||
-      (s = dalloc(d, &d->g, (size_t)d->hidden * 4)) ||
-      (s = dalloc(d, &d->u, (size_t)d->hidden * 4)) ||
+  // q|k and gate|up are contiguous so that a fused launch writes both.
+  if ((s = dalloc(d, &d->q, (size_t)(dim + kv_dim) * 4))) return s;
+  d->k = d->q + dim;
+  if ((s = dalloc(d, &d->g, (size_t)2 * d->hidden * 4))) return s;
+  d->u = d->g + d->hidden;
+  if ((s = dalloc(d, &d->v, (size_t)kv_dim * 4)) ||
       (s = dalloc(d, &d->inner, (size_t)d->hidden * 4)) ||
       (s = dalloc(d, &d->logits, (size_t)d->vocab * 4)) ||
       (s = dalloc(d, &d->st, sizeof(StepState))) ||

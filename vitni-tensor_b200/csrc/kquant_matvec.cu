@@ -524,14 +524,7 @@ __global__ void __launch_bounds__((CW + 1) * 32, VTQ_KQ_CTAS) kq_matvec_kernel(c
   }
 }
 
-bool use_pdl() {
-  static int v = -1;
-  if (v < 0) {
-    const char* e = getenv("VTQ_NO_PDL");
-    v = (e && *e && *e != '0') ? 0 : 1;
-  }
-  return v == 1;
-}
+bool use_pdl() { return pdl_enabled(); }
 
 template <int QT, int MAXB, int NCH, int CW>
 cudaError_t launch_variant(const KqParams& p, int grid, uint32_t smem, cudaStream_t st) {
@@ -573,6 +566,15 @@ cudaError_t launch_qt(const KqParams& p, int grid, uint32_t smem, cudaStream_t s
 }
 
 }  // namespace
+
+bool pdl_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("VTQ_NO_PDL");
+    v = (e && *e && *e != '0') ? 0 : 1;
+  }
+  return v == 1;
+}
 
 int num_sms() {
   static int n = 0;

@@ -76,4 +76,10 @@ cudaError_t launch_kq_or_canon(const DevMatrix& m, const float* x, float* y, uns
 int num_sms();
 int max_smem_optin();
 
+// Programmatic dependent launch for the kernels of a dependent chain (off
+// with VTQ_NO_PDL=1). A kernel launched this way may start while its
+// predecessor runs; it must execute griddepcontrol.wait before reading the
+// predecessor's outputs or writing anything the predecessor reads.
+bool pdl_enabled();
+
 }  // namespace vtq
