@@ -181,6 +181,9 @@ float vtq_powf(float x, float y);
  * (tests/transcendental_determinism.rs:36-44): expf, sqrtf(|v|), cosf, sinf,
  * powf(1e4, v/64), powf(1e6, v/64), 1/(1+expf(-v)); out holds 7*n floats. */
 void vtq_libm_sweep(const float* in, size_t n, float* out);
+/* The same sweep with expf, sqrtf and the sigmoid computed by device code
+ * (the decode kernels' functions); sin / cos / pow are host-only (RoPE tables). */
+int vtq_libm_sweep_device(const float* in, size_t n, float* out);
 
 /* ---- Row-sharded linears with the all-gather fused into the kernel ----
  * No counterpart in the reference (it is single-process; its parallel

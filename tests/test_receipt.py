@@ -36,3 +36,14 @@ def test_gguf_roundtrip_small():
                                      "vocab=300,seq=64,shared=false")
     toks = gguf.prompt_tokens(16, 300)
     assert len(toks) == 16 and min(toks) >= 3 and max(toks) <= 299
+
+
+def test_receipt_json_matches_the_reference_binary_format():
+    rc = {"model_digest": "ab" * 32, "regime": receipt.REGIME, "model_digest_v1": "cd" * 32,
+          "weights_hash": "ef" * 32, "tokens": [5, 17, 3]}
+    line = receipt.receipt_json(rc)
+    assert line == ('{"model_digest":"' + "ab" * 32 + '","regime":"' + receipt.REGIME +
+                    '","model_digest_v1":"' + "cd" * 32 + '","weights_hash":"' + "ef" * 32 +
+                    '","tokens":[5,17,3]}')
+    import json
+    assert json.loads(line)["tokens"] == [5, 17, 3]

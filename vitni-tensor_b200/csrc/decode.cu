@@ -17,6 +17,7 @@
 #include <cuda_fp16.h>
 
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <string>
@@ -286,32 +287,7 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(float* x, const float* del
   }
   __syncthreads();
   if (threadIdx.x == 0) {
-    // The reference's serial sum (rms_norm.rs:97-100): one dependent fp32 add
-    // per element. Loads run a batch ahead so the chain is add latency only.
-    float s = 0.0f;
-    const float4* q4 = reinterpret_cast<const float4*>(sq);
-    const int n4 = n / 4, nb = n4 / 8;
-    float4 a[8], b[8];
-    if (nb > 0) {
-#pragma unroll
-      for (int u = 0; u < 8; u++) a[u] = q4[u];
-    }
-    for (int c = 0; c < nb; c++) {
-      if (c + 1 < nb) {
-#pragma unroll
-        for (int u = 0; u < 8; u++) b[u] = q4[8 * (c + 1) + u];
-      }
-#pragma unroll
-      for (int u = 0; u < 8; u++) {
-        s = __fadd_rn(s, a[u].x);
-        s = __fadd_rn(s, a[u].y);
-        s = __fadd_rn(s, a[u].z);
-        s = __fadd_rn(s, a[u].w);
-      }
-#pragma unroll
-      for (int u = 0; u < 8; u++) a[u] = b[u];
-    }
-    for (int i = 32 * nb; i < n; i++) s = __fadd_rn(s, sq[i]);
+    const float s = serial_sum(sq, n);  // rms_norm.rs:97-100
     const float mean = __fdiv_rn(s, (float)n);
     s_scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
   }
@@ -321,6 +297,33 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(float* x, const float* del
     const float v = x[i];
     out[i] = __fmul_rn(__fmul_rn(v, scale), w[i]);
   }
+}
+
+// RMSNorm with the residual add written to a separate buffer:
+// v = x (+ delta) -> res; out = (v * scale) * w (rms_norm.rs:94-108).
+__global__ void __launch_bounds__(256) rmsnorm_res_kernel(const float* x, const float* delta,
+                                                          const float* w, float eps, int n,
+                                                          float* out, float* res) {
+  extern __shared__ float sq[];
+  __shared__ float s_scale;
+  pdl_wait();
+  pdl_release();
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    float v = x[i];
+    if (delta) v = __fadd_rn(v, delta[i]);
+    res[i] = v;
+    sq[i] = __fmul_rn(v, v);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const float s = serial_sum(sq, n);
+    const float mean = __fdiv_rn(s, (float)n);
+    s_scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
+  }
+  __syncthreads();
+  const float scale = s_scale;
+  for (int i = threadIdx.x; i < n; i += blockDim.x)
+    out[i] = __fmul_rn(__fmul_rn(res[i], scale), w[i]);
 }
 
 // Attention for one query head with the step's RoPE fused in
@@ -528,6 +531,9 @@ struct vtq_decode {
   float* rms_final = nullptr;
   float *rcos = nullptr, *rsin = nullptr, *kc = nullptr, *vc = nullptr;
   float *x, *xb, *q, *k, *v, *xo, *xb2, *g, *u, *inner, *logits;
+  float* xr = nullptr;  // second residual buffer (fused path: the norms alternate x <-> xr)
+  bool fused = false;   // every linear integer k-quant: norms/SwiGLU fused into the matvecs
+  int fuse_mask = 2;    // 1: attention norm, 2: FFN norm, 4: SwiGLU into the matvecs (2 measured fastest)
   float* logit_log = nullptr;
   size_t logit_log_cap = 0;
   StepState* st = nullptr;
@@ -537,6 +543,9 @@ struct vtq_decode {
   cudaGraphExec_t graph = nullptr;
   bool graph_logs = false;
   cudaEvent_t ev[4] = {};  // call start, first step, after last step, call end
+  // v runs on a second stream, concurrently with q|k (captured as a graph branch).
+  cudaStream_t side = nullptr;
+  cudaEvent_t fork = nullptr, join = nullptr;
   float ms_steps = 0.0f, ms_call = 0.0f;
   std::string err;
 };
@@ -639,17 +648,101 @@ vtq_status enqueue_step(vtq_decode* d, bool log_logits) {
   const size_t rms_smem = ((size_t)dim + 4) * 4;
   const size_t att_smem = ((size_t)3 * hs + d->seq_len) * 4;
   const float* delta = nullptr;
+  if (d->fused) {
+    // RMSNorm runs inside the matvecs that consume it (every CTA computes the
+    // serial sum while its weights stream in; CTA 0 of one launch stores the
+    // residual into the other buffer) and SwiGLU inside the down projection.
+    auto mv = [&](const DevMatrix& m, const float* x, float* y, cudaStream_t st,
+                  const KqXform* xf) {
+      return launch_kq_matvec(m, x, m.in_feat, 1, y, m.out_feat, d->status, st, nullptr, xf);
+    };
+    const int fz = d->fuse_mask;
+    for (int l = 0; l < d->n_layers; l++) {
+      auto& L = d->layers[l];
+      if (fz & 1) {
+        KqXform att;
+        att.kind = 2;
+        att.delta = delta;
+        att.nw = L.rms_att;
+        att.eps = d->rms_eps;
+        DCUDA(d, cudaEventRecord(d->fork, s));
+        DCUDA(d, cudaStreamWaitEvent(d->side, d->fork, 0));
+        DCUDA(d, mv(L.wv, d->x, d->v, d->side, &att));
+        DCUDA(d, cudaEventRecord(d->join, d->side));
+        att.res_out = d->xr;
+        DCUDA(d, mv(L.wqk, d->x, d->q, s, &att));
+        DCUDA(d, cudaStreamWaitEvent(s, d->join, 0));
+      } else {
+        // Norm kernel (residual x -> xr), then q|k and v side by side.
+        DCUDA(d, launch_pdl(rmsnorm_res_kernel, 1, 256, rms_smem, s, d->x, delta, L.rms_att,
+                            d->rms_eps, dim, d->xb, d->xr));
+        DCUDA(d, cudaEventRecord(d->fork, s));
+        DCUDA(d, cudaStreamWaitEvent(d->side, d->fork, 0));
+        DCUDA(d, mv(L.wv, d->xb, d->v, d->side, nullptr));
+        DCUDA(d, cudaEventRecord(d->join, d->side));
+        DCUDA(d, mv(L.wqk, d->xb, d->q, s, nullptr));
+        DCUDA(d, cudaStreamWaitEvent(s, d->join, 0));
+      }
+      DCUDA(d, launch_pdl(attention_rope_kernel, d->n_heads, 128, att_smem, s, d->q, d->k, d->v,
+                          d->kc, d->vc, l, d->seq_len, kv_dim, hs, kv_mul, d->rcos, d->rsin,
+                          d->st, d->xo));
+      DCUDA(d, mv(L.wo, d->xo, d->xb2, s, nullptr));
+      if (fz & 2) {
+        KqXform ffn;
+        ffn.kind = 2;
+        ffn.delta = d->xb2;
+        ffn.nw = L.rms_ffn;
+        ffn.eps = d->rms_eps;
+        ffn.res_out = d->x;
+        DCUDA(d, mv(L.w13, d->xr, d->g, s, &ffn));
+      } else {
+        DCUDA(d, launch_pdl(rmsnorm_res_kernel, 1, 256, rms_smem, s, d->xr, d->xb2, L.rms_ffn,
+                            d->rms_eps, dim, d->xb, d->x));
+        DCUDA(d, mv(L.w13, d->xb, d->g, s, nullptr));
+      }
+      if (fz & 4) {
+        KqXform sw;
+        sw.kind = 1;
+        sw.x2 = d->u;
+        DCUDA(d, mv(L.w2, d->g, d->xb2, s, &sw));
+      } else {
+        DCUDA(d, launch_pdl(swiglu_kernel, (d->hidden + 255) / 256, 256, 0, s, d->g, d->u,
+                            d->inner, d->hidden));
+        DCUDA(d, mv(L.w2, d->inner, d->xb2, s, nullptr));
+      }
+      delta = d->xb2;
+    }
+    KqXform fin;
+    fin.kind = 2;
+    fin.delta = delta;
+    fin.nw = d->rms_final;
+    fin.eps = d->rms_eps;
+    DCUDA(d, mv(d->head, d->x, d->logits, s, &fin));
+    if (log_logits)
+      DCUDA(d, launch_pdl(log_logits_kernel, (d->vocab + 255) / 256, 256, 0, s, d->logits,
+                          d->vocab, d->st, d->logit_log));
+    DCUDA(d, launch_pdl(argmax_next_kernel, 1, 1024, 0, s, d->logits, d->vocab, d->st,
+                        d->prompt, d->out_tokens));
+    DCUDA(d, cudaGetLastError());
+    return VTQ_OK;
+  }
   for (int l = 0; l < d->n_layers; l++) {
     auto& L = d->layers[l];
     DCUDA(d, launch_pdl(rmsnorm_kernel, 1, 256, rms_smem, s, d->x, delta, L.rms_att,
                         d->rms_eps, dim, d->xb));
+    // v depends only on the normed x: fork it onto the side stream so that it
+    // runs next to q|k, and join before attention.
+    DCUDA(d, cudaEventRecord(d->fork, s));
+    DCUDA(d, cudaStreamWaitEvent(d->side, d->fork, 0));
+    DCUDA(d, launch_kq_or_canon(L.wv, d->xb, d->v, d->status, d->side));
+    DCUDA(d, cudaEventRecord(d->join, d->side));
     if (L.fused_qk) {
       DCUDA(d, launch_kq_or_canon(L.wqk, d->xb, d->q, d->status, s));
     } else {
       DCUDA(d, launch_kq_or_canon(L.wq, d->xb, d->q, d->status, s));
       DCUDA(d, launch_kq_or_canon(L.wk, d->xb, d->k, d->status, s));
     }
-    DCUDA(d, launch_kq_or_canon(L.wv, d->xb, d->v, d->status, s));
+    DCUDA(d, cudaStreamWaitEvent(s, d->join, 0));
     DCUDA(d, launch_pdl(attention_rope_kernel, d->n_heads, 128, att_smem, s, d->q, d->k, d->v,
                         d->kc, d->vc, l, d->seq_len, kv_dim, hs, kv_mul, d->rcos, d->rsin, d->st,
                         d->xo));
@@ -693,6 +786,9 @@ vtq_status vtq_decode_open(vtq_ctx* ctx, int device, const uint8_t* gguf, size_t
   vtq_status s = VTQ_OK;
   cudaError_t ce = cudaSetDevice(device);
   if (ce == cudaSuccess) ce = cudaStreamCreateWithFlags(&d->stream, cudaStreamNonBlocking);
+  if (ce == cudaSuccess) ce = cudaStreamCreateWithFlags(&d->side, cudaStreamNonBlocking);
+  if (ce == cudaSuccess) ce = cudaEventCreateWithFlags(&d->fork, cudaEventDisableTiming);
+  if (ce == cudaSuccess) ce = cudaEventCreateWithFlags(&d->join, cudaEventDisableTiming);
   if (ce != cudaSuccess) {
     delete d;
     return VTQ_ERR_GPU;
@@ -817,7 +913,7 @@ vtq_status vtq_decode_open(vtq_ctx* ctx, int device, const uint8_t* gguf, size_t
   // before the first decode step.
   DCUDA(d, cudaMemsetAsync(d->kc, 0, kvb, d->stream));
   DCUDA(d, cudaMemsetAsync(d->vc, 0, kvb, d->stream));
-  float** bufs[] = {&d->x, &d->xb, &d->xo, &d->xb2};
+  float** bufs[] = {&d->x, &d->xr, &d->xb, &d->xo, &d->xb2};
   for (float** b : bufs)
     if ((s = dalloc(d, b, (size_t)dim * 4))) return s;
   // q|k and gate|up are contiguous so that a fused launch writes both.
@@ -834,6 +930,15 @@ vtq_status vtq_decode_open(vtq_ctx* ctx, int device, const uint8_t* gguf, size_t
     return s;
   DCUDA(d, cudaMemsetAsync(d->status, 0, 16, d->stream));
   DCUDA(d, cudaStreamSynchronize(d->stream));
+  // Fused step when every linear runs on the integer k-quant matvec and the
+  // activation row fits the matvec's shared-memory staging.
+  auto kq = [](const DevMatrix& m) { return m.dtype == T_Q4_K || m.dtype == T_Q6_K; };
+  d->fused = kq(d->head) && dim % 256 == 0 && d->hidden % 256 == 0 && dim * 4 <= 65536 &&
+             d->hidden * 4 <= 65536 && getenv("VTQ_DECODE_UNFUSED") == nullptr;
+  if (const char* e = getenv("VTQ_DECODE_FUSE")) d->fuse_mask = atoi(e) & 7;
+  for (auto& L : d->layers)
+    d->fused = d->fused && L.fused_qk && L.fused_13 && kq(L.wqk) && kq(L.wv) && kq(L.wo) &&
+               kq(L.w13) && kq(L.w2);
   return VTQ_OK;
 }
 
@@ -941,8 +1046,12 @@ vtq_status vtq_decode_close(vtq_decode* d) {
   if (d->graph) cudaGraphExecDestroy(d->graph);
   for (auto e : d->ev)
     if (e) cudaEventDestroy(e);
+  if (d->side) cudaStreamSynchronize(d->side);
+  if (d->fork) cudaEventDestroy(d->fork);
+  if (d->join) cudaEventDestroy(d->join);
   for (void* p : d->allocs) cudaFree(p);
   if (d->stream) cudaStreamDestroy(d->stream);
+  if (d->side) cudaStreamDestroy(d->side);
   delete d;
   return VTQ_OK;
 }

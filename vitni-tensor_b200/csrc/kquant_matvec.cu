@@ -30,6 +30,7 @@
 //    pairing is identical to the reference's level-wise loop.
 #include "vtq_device.cuh"
 #include "vtq_internal.h"
+#include "vtq_libm.h"
 #include <cuda_fp16.h>
 
 namespace vtq {
@@ -57,6 +58,8 @@ __device__ const float* g_kq_trace_y[8];
 #define KQ_TRACE(slot) (void)0
 #endif
 
+constexpr uint32_t kScaleOff = 448;  // inside the 512-byte head, above the barriers
+
 struct KqParams {
   const float* x;
   int64_t ldx;
@@ -75,6 +78,8 @@ struct KqParams {
   uint32_t off_xd, off_bsum, off_xq, off_xf, off_stage;
   unsigned* status;
   GatherTarget g;           // g.world > 0: fused all-gather of y to every rank
+  KqXform xf;               // activation transform (batch 1; kind 2 needs x_smem)
+  uint32_t off_xsq;         // kind 2: squares of v (n floats)
 };
 
 // quantize_block_q8 for every (batch row, superblock): one warp per block,
@@ -83,7 +88,8 @@ struct KqParams {
 // the TMA-staged rows in shared memory (row stride n) or global x (ldx).
 template <int NB, int CW>
 __device__ __forceinline__ void quantize_x(const KqParams& p, const float* xs, int64_t lds,
-                                           int warp, int lane, float* xd, int* bsum, int8_t* xq) {
+                                           int warp, int lane, float* xd, int* bsum, int8_t* xq,
+                                           float xscale) {
   const int nblk = p.batch * p.S;
   for (int u = warp; u < nblk; u += CW) {
     const int b = u / p.S, s = u - b * p.S;
@@ -97,6 +103,18 @@ __device__ __forceinline__ void quantize_x(const KqParams& p, const float* xs, i
     } else {
 #pragma unroll
       for (int i = 0; i < 8; i++) v[i] = src[i];
+    }
+    if (p.xf.kind == 1) {  // SwiGLU: silu(g) * up
+      const float* up = p.xf.x2 + s * 256 + lane * 8;
+#pragma unroll
+      for (int i = 0; i < 8; i++) {
+        const float silu = __fdiv_rn(v[i], __fadd_rn(1.0f, libm::expf(-v[i])));
+        v[i] = __fmul_rn(silu, up[i]);
+      }
+    } else if (p.xf.kind == 2) {  // RMSNorm output (v already holds x + delta)
+      const float* nw = p.xf.nw + s * 256 + lane * 8;
+#pragma unroll
+      for (int i = 0; i < 8; i++) v[i] = __fmul_rn(__fmul_rn(v[i], xscale), nw[i]);
     }
     // amax = max over non-NaN |v|, starting at +0.0 (quant.rs:752-758).
     uint32_t am = 0;
@@ -468,7 +486,32 @@ __global__ void __launch_bounds__((CW + 1) * 32, VTQ_KQ_CTAS) kq_matvec_kernel(c
   } else {
     grid_dep_wait();
   }
-  quantize_x<QT == 0 ? 8 : 16, CW>(p, xs, xstride, warp, lane, xd, bsum, xq);
+  float xscale = 0.0f;
+  if (p.xf.kind == 2) {
+    // Fused RMSNorm: v = x (+ delta) in place, squares beside it, then the
+    // serial sum on one thread while the weight stages keep streaming in.
+    float* xsq = reinterpret_cast<float*>(smem + p.off_xsq);
+    // The scale lives in the reserved head of the dynamic block (after the
+    // barriers): no static shared memory, so the dynamic size may use the
+    // whole opt-in limit.
+    float& s_scale = *reinterpret_cast<float*>(smem + kScaleOff);
+    for (int i = tid; i < p.n; i += CW * 32) {
+      float v = xf[i];
+      if (p.xf.delta) v = __fadd_rn(v, p.xf.delta[i]);
+      xf[i] = v;
+      xsq[i] = __fmul_rn(v, v);
+      if (p.xf.res_out && blockIdx.x == 0) p.xf.res_out[i] = v;
+    }
+    asm volatile("bar.sync 1, %0;" ::"n"(CW * 32));
+    if (tid == 0) {
+      const float sum = serial_sum(xsq, p.n);
+      const float mean = __fdiv_rn(sum, (float)p.n);
+      s_scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, p.xf.eps)));
+    }
+    asm volatile("bar.sync 1, %0;" ::"n"(CW * 32));
+    xscale = s_scale;
+  }
+  quantize_x<QT == 0 ? 8 : 16, CW>(p, xs, xstride, warp, lane, xd, bsum, xq, xscale);
   asm volatile("bar.sync 1, %0;" ::"n"(CW * 32));
   if (tid == 0) KQ_TRACE(2);
 
@@ -600,7 +643,7 @@ static inline uint32_t align_up(uint32_t v, uint32_t a) { return (v + a - 1) / a
 
 cudaError_t launch_kq_matvec(const DevMatrix& m, const float* x, int64_t ldx, int64_t batch,
                              float* y, int64_t ldy, unsigned* status, cudaStream_t st,
-                             const GatherTarget* g) {
+                             const GatherTarget* g, const KqXform* xform) {
   constexpr int KQ_BMAX = 4;  // activation rows per launch
   if (m.dtype != T_Q4_K && m.dtype != T_Q6_K) return cudaErrorInvalidValue;
   const int S = (int)(m.in_feat / 256);
@@ -639,10 +682,15 @@ cudaError_t launch_kq_matvec(const DevMatrix& m, const float* x, int64_t ldx, in
       if (g->world < 1 || g->world > kMaxRanks || batch > KQ_BMAX) return cudaErrorInvalidValue;
       p.g = *g;
     }
+    if (xform && xform->kind) {
+      if (batch != 1 || (xform->kind == 1 && !xform->x2) || (xform->kind == 2 && !xform->nw))
+        return cudaErrorInvalidValue;
+      p.xf = *xform;
+    }
     p.lpr = lpr;
     const int NB = m.dtype == T_Q4_K ? BsumStride<8>::v : BsumStride<16>::v;
     constexpr uint32_t kBarBytes = (2 * KQ_NST_MAX + 1) * 8;  // full[], empty[], xbar
-    static_assert(kBarBytes <= 512, "barrier area");
+    static_assert(kBarBytes <= kScaleOff && kScaleOff + 4 <= 512, "barrier area");
     uint32_t off = 512;  // mbarriers (kBarBytes) live below this offset
     p.off_xd = off;
     off = align_up(off + nb * S * 4, 16);
@@ -656,6 +704,11 @@ cudaError_t launch_kq_matvec(const DevMatrix& m, const float* x, int64_t ldx, in
                 xbytes <= (uint32_t)VTQ_KQ_XMAX) ? 1 : 0;
     p.off_xf = off;
     if (p.x_smem) off = align_up(off + xbytes, 128);
+    if (p.xf.kind == 2) {
+      if (!p.x_smem) return cudaErrorInvalidValue;  // the fused norm works on the staged row
+      p.off_xsq = off;
+      off = align_up(off + (uint32_t)p.n * 4, 128);
+    }
     p.off_stage = off;
     // Stages of ~24 KB of whole warp passes (TMA streams at full rate from 16 KB).
     const int rows_per_cta = p.rows_base + (p.rows_rem ? 1 : 0);

@@ -135,4 +135,42 @@ __device__ __forceinline__ int q8_round(float scaled) {
   return max(-127, min(127, q));
 }
 
+// The reference's serial fp32 sum of n values in shared memory (rms_norm.rs:
+// 97-100: one dependent add per element, left to right). Two register batches
+// of 32 in ping-pong keep the next loads in flight while the current batch is
+// added, so the chain runs at add latency. `v` must be 16-byte aligned.
+__device__ __forceinline__ float serial_sum(const float* v, int n) {
+  float s = 0.0f;
+  const float4* q4 = reinterpret_cast<const float4*>(v);
+  const int nb = n / 32;
+  float4 a[8], b[8];
+  auto add8 = [&](const float4 (&w)[8]) {
+#pragma unroll
+    for (int u = 0; u < 8; u++) {
+      s = __fadd_rn(s, w[u].x);
+      s = __fadd_rn(s, w[u].y);
+      s = __fadd_rn(s, w[u].z);
+      s = __fadd_rn(s, w[u].w);
+    }
+  };
+  if (nb > 0) {
+#pragma unroll
+    for (int u = 0; u < 8; u++) a[u] = q4[u];
+  }
+  for (int c = 0; c < nb; c += 2) {
+    if (c + 1 < nb) {
+#pragma unroll
+      for (int u = 0; u < 8; u++) b[u] = q4[8 * (c + 1) + u];
+    }
+    add8(a);
+    if (c + 2 < nb) {
+#pragma unroll
+      for (int u = 0; u < 8; u++) a[u] = q4[8 * (c + 2) + u];
+    }
+    if (c + 1 < nb) add8(b);
+  }
+  for (int i = 32 * nb; i < n; i++) s = __fadd_rn(s, v[i]);
+  return s;
+}
+
 }  // namespace vtq

@@ -45,12 +45,28 @@ struct GatherTarget {
   unsigned* done;
 };
 
+// Transform applied to a batch-1 activation row while the matvec quantises it
+// (decode fusion; each is the reference's op order):
+//   kind 1 SwiGLU  x_i = silu(x_i) * x2_i, silu(g) = g / (1 + expf(-g))
+//                  (forward_quantized.rs:556-561)
+//   kind 2 RMSNorm v_i = x_i (+ delta_i); x_i = (v_i * scale) * nw_i with
+//                  scale = 1 / sqrtf(sum(v^2) / n + eps), the sum serial
+//                  (rms_norm.rs:94-108); CTA 0 stores v to res_out if set.
+struct KqXform {
+  int kind = 0;
+  const float* x2 = nullptr;
+  const float* delta = nullptr;
+  const float* nw = nullptr;
+  float eps = 0.0f;
+  float* res_out = nullptr;
+};
+
 // Integer k-quant matvec (Q4_K / Q6_K against int8-quantised activations):
 // y[b, r] for r in [0, R), b in [0, batch). x row stride ldx, y row stride ldy.
 // With `g`, y/ldy are ignored and the rows go to every rank of g instead.
 cudaError_t launch_kq_matvec(const DevMatrix& m, const float* x, int64_t ldx, int64_t batch,
                              float* y, int64_t ldy, unsigned* status, cudaStream_t st,
-                             const GatherTarget* g = nullptr);
+                             const GatherTarget* g = nullptr, const KqXform* xf = nullptr);
 
 // Waits on `st` until this rank's arrival counter has received `signals` more
 // arrivals than before (`expected` is a device counter of arrivals consumed).

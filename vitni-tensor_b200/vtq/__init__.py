@@ -39,7 +39,7 @@ EXPORTS = (
     "vtq_decode_config", "vtq_decode_run", "vtq_decode_close", "vtq_expf", "vtq_sinf",
     "vtq_cosf", "vtq_powf", "vtq_libm_sweep", "vtq_linear_host_noalloc",
     "vtq_gather_create", "vtq_gather_connect", "vtq_gather_y", "vtq_linear_gather",
-    "vtq_gather_wait", "vtq_gather_destroy",
+    "vtq_gather_wait", "vtq_gather_destroy", "vtq_libm_sweep_device",
     "vtq_decode_timing", "vtq_decode_debug_buffer",
 )
 
@@ -138,6 +138,7 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         "vtq_linear_gather": (c_i32, [c_p, c_p, c_p, c_i64, c_p, c_i64, c_i64, c_i64, c_u32]),
         "vtq_gather_wait": (c_i32, [c_p, c_p, c_u32]),
         "vtq_gather_destroy": (c_i32, [c_p]),
+        "vtq_libm_sweep_device": (c_i32, [c_p, c_sz, c_p]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)

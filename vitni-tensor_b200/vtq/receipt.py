@@ -66,3 +66,12 @@ def decode_receipt(model_id: str, gguf_blob: bytes, arch: str, prompt, n_new: in
     return {"model_digest": digest_v2(inputs, outputs).hex(), "regime": REGIME,
             "model_digest_v1": digest_v1(inputs, outputs).hex(),
             "weights_hash": weights_hash.hex(), "tokens": [int(t) for t in generated]}
+
+
+def receipt_json(rc: dict) -> str:
+    """The receipt line exactly as the reference's binary prints it
+    (src/bin/vitni-receipt.rs:46-53): compact JSON, this key order."""
+    toks = ",".join(str(int(t)) for t in rc["tokens"])
+    return ('{"model_digest":"%s","regime":"%s","model_digest_v1":"%s","weights_hash":"%s",'
+            '"tokens":[%s]}' % (rc["model_digest"], rc["regime"], rc["model_digest_v1"],
+                                rc["weights_hash"], toks))
