@@ -501,58 +501,87 @@ def run_decode(args, world, rank, local):
 
 
 def run_sharded(args, world, rank, local, ctx, stream, cfg):
-    """N > 1: every matvec's output rows are split into contiguous ranges, one per
-    rank; a step is the local matvec plus an NCCL all-gather of y over NVLink
-    (strong scaling: the job's total work is the N = 1 workload)."""
+    """N > 1: every matvec is row-sharded over the ranks and y is reassembled on
+    every rank inside the timed region.
+
+    Default (weak scaling): each rank owns a full-size shard -- the configured
+    matrix -- of a matrix N times taller (rank 0's shard is the N = 1 matrix,
+    rank r's is drawn with its own seed), so per-GPU work stays fixed as N
+    grows and the all-gather moves N times the rows. --strong: the configured
+    matrix itself is split into N contiguous row ranges (fixed total work)."""
     import torch
     import torch.distributed as dist
     import vtq
     from vtq import synth, shard
-    host_w = [synth.weight(dt, f"{args.config}.w.{n}x{r}", r, n) for dt, n, r in cfg]
+    strong = args.strong
     host_x = [synth.activation(f"{args.config}.x.{n}", 1, n) for dt, n, r in cfg]
-    rng = [shard.row_range(r, world, rank) for dt, n, r in cfg]
-    for (dt, n, r) in cfg:
-        if r % world:
-            raise SystemExit(f"{args.config}: {r} rows do not split evenly over {world} ranks")
+    if strong:
+        for (dt, n, r) in cfg:
+            if r % world:
+                raise SystemExit(f"{args.config}: {r} rows do not split evenly over {world} ranks")
+        host_w = [synth.weight(dt, f"{args.config}.w.{n}x{r}", r, n) for dt, n, r in cfg]
+        rows_log = [r for dt, n, r in cfg]
+        rng = [shard.row_range(r, world, rank) for dt, n, r in cfg]
+    else:
+        tag = f".rank{rank}" if rank else ""
+        host_w = [synth.weight(dt, f"{args.config}.w.{n}x{r}{tag}", r, n) for dt, n, r in cfg]
+        rows_log = [r * world for dt, n, r in cfg]
+        rng = [(rank * r, (rank + 1) * r) for dt, n, r in cfg]
     wbytes = sum((b - a) * vtq.row_bytes(dt, n) for (dt, n, r), (a, b) in zip(cfg, rng))
     copies = max(1, -(-ROTATE_MIN_BYTES // wbytes))
-    weights = [[ctx.upload(dt, host_w[i], n, r, *rng[i]) for i, (dt, n, r) in enumerate(cfg)]
-               for _ in range(copies)]
+    if strong:
+        weights = [[ctx.upload(dt, host_w[i], n, r, *rng[i]) for i, (dt, n, r) in enumerate(cfg)]
+                   for _ in range(copies)]
+    else:
+        weights = [[ctx.upload(dt, host_w[i], n, r) for i, (dt, n, r) in enumerate(cfg)]
+                   for _ in range(copies)]
     xs = [torch.from_numpy(x).cuda() for x in host_x]
     ys = [torch.empty(b - a, device="cuda") for a, b in rng]
     fused = all(dt in (vtq.Q4_K, vtq.Q6_K) for dt, n, r in cfg) and world <= 8 and \
         os.environ.get("VTQ_GATHER", "fused") == "fused"
-    offs = [sum(r for _, _, r in cfg[:i]) for i in range(len(cfg))]
+    offs = [sum(rows_log[:i]) for i in range(len(cfg))]
     if fused:
         # Fused path: each matvec stores its rows into every rank's full y over
         # NVLink; one bounded wait per step for world x len(cfg) arrivals.
-        gat = vtq.Gather(ctx, sum(r for _, _, r in cfg))
-        full = [device_view(gat.y_ptr + 4 * offs[i], r) for i, (dt, n, r) in enumerate(cfg)]
+        gat = vtq.Gather(ctx, sum(rows_log))
+        full = [device_view(gat.y_ptr + 4 * offs[i], rows_log[i]) for i in range(len(cfg))]
     else:
-        full = [torch.empty(r, device="cuda") for dt, n, r in cfg]
+        full = [torch.empty(rl, device="cuda") for rl in rows_log]
 
     def step(c):
         for i in range(len(cfg)):
             if fused:
-                gat.linear(weights[c][i], xs[i].data_ptr(), rng[i][0], cfg[i][2], offs[i])
+                # The step's last matvec ends with the wait for every rank's rows.
+                last = i == len(cfg) - 1
+                gat.linear(weights[c][i], xs[i].data_ptr(), rng[i][0], rows_log[i], offs[i],
+                           wait_signals=world * len(cfg) if last else 0)
             else:
                 ctx.linear_ptr(weights[c][i], xs[i].data_ptr(), ys[i].data_ptr(), 1)
                 dist.all_gather_into_tensor(full[i], ys[i])
-        if fused:
-            gat.wait(world * len(cfg))
 
     for c in range(copies):
         step(c)
     torch.cuda.synchronize()
-    # Shard invariance: the gathered y equals the oracle's full y bit for bit.
+    # Parity. Strong: the gathered y equals the oracle's full y bit for bit on
+    # every rank. Weak: this rank's rows of the gathered y equal the oracle for
+    # its shard, and every rank holds the same gathered y (bit checksum).
     from oracle import oracle as O
+    threads = max(1, (os.cpu_count() or 1) // world)
     for i, (dt, n, r) in enumerate(cfg):
         name = {12: "q4_k_integer", 14: "q6_k_integer"}.get(dt)
-        ref = O.linear(name, host_x[i], host_w[i], 1, n, r, os.cpu_count()) if name else \
-            O.linear_dispatch(dt, host_x[i], host_w[i], n, r, threads=os.cpu_count())
+        ref = O.linear(name, host_x[i], host_w[i], 1, n, r, threads) if name else \
+            O.linear_dispatch(dt, host_x[i], host_w[i], n, r, threads=threads)
         got = full[i].cpu().numpy()
-        if not np.array_equal(got.view(np.uint32), ref.view(np.uint32)):
+        mine = got if strong else got[rng[i][0]:rng[i][1]]
+        if not np.array_equal(mine.view(np.uint32), ref.view(np.uint32)):
             raise SystemExit(f"rank {rank}: sharded result differs from the oracle ({args.config})")
+        bits = torch.tensor([int(got.view(np.uint32).astype(np.uint64).sum() % (1 << 62))],
+                            dtype=torch.int64, device="cuda")
+        hi, lo = bits.clone(), bits.clone()
+        dist.all_reduce(hi, op=dist.ReduceOp.MAX)
+        dist.all_reduce(lo, op=dist.ReduceOp.MIN)
+        if int(hi.item()) != int(lo.item()):
+            raise SystemExit(f"rank {rank}: ranks hold different gathered y ({args.config})")
     steps = max(copies, min(args.steps, 2000)) // copies * copies
     for i in range(max(3, args.warmup)):
         step(i % copies)
@@ -585,7 +614,7 @@ def run_sharded(args, world, rank, local, ctx, stream, cfg):
     ms = torch.tensor([e0.elapsed_time(e1)], device="cuda")
     dist.all_reduce(ms, op=dist.ReduceOp.MAX)
     ms = float(ms.item())
-    step_bytes = sum(algo_bytes(dt, n, r) for dt, n, r in cfg)
+    step_bytes = sum(algo_bytes(dt, n, r) for dt, n, r in cfg) * (1 if strong else world)
     value = step_bytes * steps / (ms / 1e3) / 1e9
     # Local kernel time alone (no collective), for the roofline of the shard.
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
@@ -602,10 +631,10 @@ def run_sharded(args, world, rank, local, ctx, stream, cfg):
         (b - a) * vtq.row_bytes(dt, n) + 4 * n + 4 * (b - a) for (dt, n, r), (a, b) in zip(cfg, rng))
     peak, peak_kind = peaks()
     achieved = local_bytes / (statistics.mean(durs) / 1e3) / 1e9
-    gather_bytes = sum(4 * r for dt, n, r in cfg)
+    gather_bytes = sum(4 * rl for rl in rows_log)
     # e2e: pinned host x -> device, local matvec, all-gather, full y -> pinned host.
     px = [torch.from_numpy(x).pin_memory() for x in host_x]
-    py = [torch.empty(r, dtype=torch.float32).pin_memory() for dt, n, r in cfg]
+    py = [torch.empty(rl, dtype=torch.float32).pin_memory() for rl in rows_log]
     e2e_steps = max(20, min(1000, steps // 2))
     dist.barrier()
     torch.cuda.synchronize()
@@ -615,12 +644,11 @@ def run_sharded(args, world, rank, local, ctx, stream, cfg):
         for i in range(len(cfg)):
             xs[i].copy_(px[i], non_blocking=True)
             if fused:
-                gat.linear(weights[k % copies][i], xs[i].data_ptr(), rng[i][0], cfg[i][2], offs[i])
+                gat.linear(weights[k % copies][i], xs[i].data_ptr(), rng[i][0], rows_log[i],
+                           offs[i], wait_signals=world * len(cfg) if i == len(cfg) - 1 else 0)
             else:
                 ctx.linear_ptr(weights[k % copies][i], xs[i].data_ptr(), ys[i].data_ptr(), 1)
                 dist.all_gather_into_tensor(full[i], ys[i])
-        if fused:
-            gat.wait(world * len(cfg))
         for i in range(len(cfg)):
             py[i].copy_(full[i], non_blocking=True)
     f1.record(stream)
@@ -629,16 +657,19 @@ def run_sharded(args, world, rank, local, ctx, stream, cfg):
     dist.all_reduce(ems, op=dist.ReduceOp.MAX)
     e2e = {"value": round(step_bytes * e2e_steps / (float(ems.item()) / 1e3) / 1e9, 2),
            "unit": "GB/s", "h2d_bytes_per_step": sum(4 * n for dt, n, r in cfg),
-           "d2h_bytes_per_step": sum(4 * r for dt, n, r in cfg), "steps": e2e_steps}
+           "d2h_bytes_per_step": sum(4 * rl for rl in rows_log), "steps": e2e_steps}
     if rank == 0:
         print(json.dumps({
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
             "steps": steps, "warmup": max(3, args.warmup), "ms_per_step": round(ms / steps, 5),
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8",
-            "data": "synthetic",
+            "higher_is_better": True, "scaling": "strong" if strong else "weak",
+            "vs_baseline": None, "dtype": "int8", "data": "synthetic",
             "config": {"workload": args.config,
                        "matvecs": [f"{vtq.formats.NAMES[dt]} {n}->{r}" for dt, n, r in cfg],
-                       "batch": 1, "parallelism": f"rows sharded x{world} + " + ("fused NVLink all-gather (each matvec stores its rows into every rank's y)" if fused else "NCCL all-gather of y"),
+                       "batch": 1,
+                       "shards": ("the configured matrices split over the ranks" if strong else
+                                  "each rank: a full-size shard of an N-times taller matrix"),
+                       "parallelism": f"rows sharded x{world} + " + ("fused NVLink all-gather (each matvec stores its rows into every rank's y)" if fused else "NCCL all-gather of y"),
                        "l2": f"inputs larger than L2: {copies} rotating weight copies per rank "
                              f"({copies * wbytes / 1e6:.0f} MB)",
                        "timing": ("CUDA graph of one rotation (fused matvec+gather kernels and the "
@@ -680,6 +711,11 @@ def main():
     ap.add_argument("--config", default="c2_q4_k_llama7b_ffn")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--check", action="store_true", help="bit-compare outputs with the oracle")
+    ap.add_argument("--sharded", action="store_true",
+                    help="run the row-sharded path (fused gather) even with one rank")
+    ap.add_argument("--strong", action="store_true",
+                    help="N > 1: split the configured matrices over the ranks (fixed total work) "
+                         "instead of one full-size shard per rank")
     ap.add_argument("--launches-only", action="store_true",
                     help="profiling mode: one weight copy, W + K plain launches per matvec, "
                          "no graph, no timing output (for ncu captures)")
@@ -711,7 +747,12 @@ def main():
     ctx.set_stream(stream.cuda_stream)
 
     cfg = synth.CONFIGS[args.config]
-    if world > 1:
+    if world > 1 or args.sharded:
+        if not dist.is_initialized():
+            os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+            os.environ.setdefault("MASTER_PORT", "29533")
+            dist.init_process_group("nccl", rank=0, world_size=1,
+                                    device_id=torch.device("cuda", local))
         run_sharded(args, world, rank, local, ctx, stream, cfg)
         return
     step_bytes = sum(algo_bytes(dt, n, r) for dt, n, r in cfg)

@@ -205,6 +205,12 @@ vtq_status vtq_linear_gather(vtq_ctx* ctx, const vtq_weight* w, const float* x, 
                              vtq_gather* g, int64_t y_offset, int64_t ldy, int64_t row0,
                              uint32_t flags);
 vtq_status vtq_gather_wait(vtq_ctx* ctx, vtq_gather* g, uint32_t signals);
+/* vtq_linear_gather whose launch also ends with the wait for `wait_signals`
+ * arrivals (no separate wait launch; use it for the last gathered linear
+ * before y is read). */
+vtq_status vtq_linear_gather_wait(vtq_ctx* ctx, const vtq_weight* w, const float* x,
+                                  int64_t batch, vtq_gather* g, int64_t y_offset, int64_t ldy,
+                                  int64_t row0, uint32_t flags, uint32_t wait_signals);
 vtq_status vtq_gather_destroy(vtq_gather* g);
 
 #ifdef __cplusplus

@@ -37,10 +37,14 @@ def _rank(rank, port, q):
             xs.append(torch.from_numpy(x).cuda())
             name = "q4_k_integer" if dt == 12 else "q6_k_integer"
             refs.append(O.linear(name, x, w, 1, n, r, 8))
-        for step in range(3):  # counters keep growing across steps
+        for step in range(4):  # counters keep growing across steps
+            inline = step % 2 == 1  # odd steps: the last launch waits itself
             for i, (dt, n, r) in enumerate(SHAPES):
-                gat.linear(ws[i][0], xs[i].data_ptr(), ws[i][1], r, offs[i])
-            gat.wait(WORLD * len(SHAPES))
+                last = i == len(SHAPES) - 1
+                gat.linear(ws[i][0], xs[i].data_ptr(), ws[i][1], r, offs[i],
+                           wait_signals=WORLD * len(SHAPES) if (inline and last) else 0)
+            if not inline:
+                gat.wait(WORLD * len(SHAPES))
             ctx.synchronize()
             class _View:  # zero-copy torch view of the gather buffer
                 __cuda_array_interface__ = {"shape": (total,), "typestr": "<f4",

@@ -17,6 +17,10 @@ namespace {
 
 __global__ void gather_wait_kernel(const unsigned* cnt, unsigned* expected, unsigned signals,
                                    unsigned* status) {
+  // Programmatic launch: wait for this rank's gathered launches to finish,
+  // let the next kernel start streaming its weights, then wait for the peers.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   if (threadIdx.x != 0) return;
   const unsigned target = *expected + signals;
   *expected = target;
@@ -37,8 +41,17 @@ __global__ void gather_wait_kernel(const unsigned* cnt, unsigned* expected, unsi
 
 cudaError_t launch_gather_wait(unsigned* cnt, unsigned* expected, unsigned signals,
                                unsigned* status, cudaStream_t st) {
-  gather_wait_kernel<<<1, 32, 0, st>>>(cnt, expected, signals, status);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(1);
+  cfg.blockDim = dim3(32);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, gather_wait_kernel, (const unsigned*)cnt, expected, signals,
+                            status);
 }
 
 }  // namespace vtq

@@ -79,6 +79,7 @@ struct KqParams {
   unsigned* status;
   GatherTarget g;           // g.world > 0: fused all-gather of y to every rank
   KqXform xf;               // activation transform (batch 1; kind 2 needs x_smem)
+  uint32_t off_ystage;      // gather: this CTA's finished rows [batch][rows_base + 1]
   uint32_t off_xsq;         // kind 2: squares of v (n floats)
 };
 
@@ -347,7 +348,8 @@ __device__ __forceinline__ float seg_fixed_tree(float (&v)[NCH], int sl, int lpr
 template <int QT, int MAXB, int NCH>
 __device__ __forceinline__ void consume_pass(const KqParams& p, const uint8_t* sbuf, int rr,
                                              bool row_ok, int sl, int64_t yrow,
-                                             const int8_t* xq, const float* xd, const int* bsum) {
+                                             const int8_t* xq, const float* xd, const int* bsum,
+                                             float* ystage, int64_t ycta0) {
   float part[NCH][MAXB];
 #pragma unroll
   for (int c = 0; c < NCH; c++) {
@@ -373,16 +375,10 @@ __device__ __forceinline__ void consume_pass(const KqParams& p, const uint8_t* s
       for (int c = 0; c < NCH; c++) v[c] = part[c][b];
       const float t = seg_fixed_tree<NCH>(v, sl, p.lpr, p.S);
       if (row_ok && sl == 0) {
-        if (p.g.world == 0) {
+        if (p.g.world == 0)
           p.y[(int64_t)b * p.ldy + yrow] = t;
-        } else {
-          // Row-sharded linear: store this row into every rank's full y
-          // (peer memory over NVLink for q != this rank).
-          const int64_t at = (int64_t)b * p.g.ldy + p.g.row0 + yrow;
-#pragma unroll
-          for (int q = 0; q < kMaxRanks; q++)
-            if (q < p.g.world) p.g.y[q][at] = t;
-        }
+        else  // row-sharded: stage; warp 0 sends the CTA's rows at the end
+          ystage[b * (p.rows_base + 1) + (int)(yrow - ycta0)] = t;
       }
     }
   }
@@ -412,6 +408,7 @@ __global__ void __launch_bounds__((CW + 1) * 32, VTQ_KQ_CTAS) kq_matvec_kernel(c
   int* bsum = reinterpret_cast<int*>(smem + p.off_bsum);
   int8_t* xq = reinterpret_cast<int8_t*>(smem + p.off_xq);
   float* xf = reinterpret_cast<float*>(smem + p.off_xf);
+  float* ystage = reinterpret_cast<float*>(smem + p.off_ystage);
   uint8_t* stg = smem + p.off_stage;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -538,7 +535,8 @@ __global__ void __launch_bounds__((CW + 1) * 32, VTQ_KQ_CTAS) kq_matvec_kernel(c
       const uint8_t* sbuf = stg + (size_t)buf * p.stage_bytes;
       for (; g < gend; g += CW) {
         const int r = g * rpw + seg;  // CTA-local row
-        consume_pass<QT, MAXB, NCH>(p, sbuf, r - k * p.rps, r < nrows, sl, r0 + r, xq, xd, bsum);
+        consume_pass<QT, MAXB, NCH>(p, sbuf, r - k * p.rps, r < nrows, sl, r0 + r, xq, xd, bsum,
+                                    ystage, r0);
       }
     }
     __syncwarp();
@@ -549,19 +547,53 @@ __global__ void __launch_bounds__((CW + 1) * 32, VTQ_KQ_CTAS) kq_matvec_kernel(c
   }
   if (tid == 0) KQ_TRACE(5);
   if (p.g.world > 0) {
-    // Publish: every storing thread fences at system scope, then the last CTA
-    // of the launch (completion counter in this rank's memory) signals every
-    // rank's arrival counter once.
-    __threadfence_system();
+    // Send: after every consumer has staged its rows, warp 0 writes the CTA's
+    // contiguous rows into every rank's y (coalesced, over NVLink for peers).
+    // The launch's last CTA (completion counter in this rank's memory) then
+    // fences at system scope, signals every rank once and, if asked, waits
+    // for the other ranks.
     asm volatile("bar.sync 1, %0;" ::"n"(CW * 32));
-    if (tid == 0) {
-      const unsigned prev = atomicAdd(p.g.done, 1u);
-      if (prev == gridDim.x - 1) {
-        *p.g.done = 0;  // every CTA of this launch has counted
-        __threadfence_system();
+    if (warp == 0) {
+      for (int b = 0; b < p.batch; b++)
+        for (int i = lane; i < nrows; i += 32) {
+          const float v = ystage[b * (p.rows_base + 1) + i];
+          const int64_t at = (int64_t)b * p.g.ldy + p.g.row0 + r0 + i;
 #pragma unroll
-        for (int q = 0; q < kMaxRanks; q++)
-          if (q < p.g.world) atomicAdd_system(p.g.cnt[q], 1u);
+          for (int q = 0; q < kMaxRanks; q++)
+            if (q < p.g.world) p.g.y[q][at] = v;
+        }
+      // Ordering: each CTA's stores reach lane 0 through __syncwarp, lane 0's
+      // acq_rel add on the completion counter (GPU scope) chains every CTA
+      // into the last one, whose system-scope fence then covers all of them
+      // before the arrival signals (causality order is transitive).
+      __syncwarp();
+      if (lane == 0) {
+        unsigned prev;
+        asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(prev) : "l"(p.g.done)
+                     : "memory");
+        if (prev == gridDim.x - 1) {
+          *p.g.done = 0;  // every CTA of this launch has counted
+          __threadfence_system();
+#pragma unroll
+          for (int q = 0; q < kMaxRanks; q++)
+            if (q < p.g.world) atomicAdd_system(p.g.cnt[q], 1u);
+          if (p.g.wait_signals) {
+            const unsigned target = *p.g.expected + p.g.wait_signals;
+            *p.g.expected = target;
+            const uint64_t t0 = globaltimer();
+            for (;;) {
+              unsigned v;
+              asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p.g.my_cnt)
+                           : "memory");
+              if ((int)(v - target) >= 0) break;
+              if (globaltimer() - t0 > VTQ_WAIT_LIMIT_NS) {
+                record_error(p.status, KERR_TIMEOUT);
+                break;
+              }
+            }
+            __threadfence_system();
+          }
+        }
       }
     }
   }
@@ -708,6 +740,10 @@ cudaError_t launch_kq_matvec(const DevMatrix& m, const float* x, int64_t ldx, in
       if (!p.x_smem) return cudaErrorInvalidValue;  // the fused norm works on the staged row
       p.off_xsq = off;
       off = align_up(off + (uint32_t)p.n * 4, 128);
+    }
+    if (p.g.world > 0) {
+      p.off_ystage = off;
+      off = align_up(off + (uint32_t)(nb * (p.rows_base + 1)) * 4, 128);
     }
     p.off_stage = off;
     // Stages of ~24 KB of whole warp passes (TMA streams at full rate from 16 KB).

@@ -467,9 +467,9 @@ float* vtq_gather_y(vtq_gather* g) {
   return g ? reinterpret_cast<float*>(g->base + kGatherHdr) : nullptr;
 }
 
-vtq_status vtq_linear_gather(vtq_ctx* c, const vtq_weight* w, const float* x, int64_t batch,
-                             vtq_gather* g, int64_t y_offset, int64_t ldy, int64_t row0,
-                             uint32_t flags) {
+vtq_status vtq_linear_gather_wait(vtq_ctx* c, const vtq_weight* w, const float* x,
+                                  int64_t batch, vtq_gather* g, int64_t y_offset, int64_t ldy,
+                                  int64_t row0, uint32_t flags, uint32_t wait_signals) {
   if (!c || !w || !x || !g) return fail(c, VTQ_ERR_INVALID_ARG, "null argument");
   for (int q = 0; q < g->world; q++)
     if (!g->peer[q]) return fail(c, VTQ_ERR_INVALID_ARG, "vtq_linear_gather: gather not connected");
@@ -493,9 +493,18 @@ vtq_status vtq_linear_gather(vtq_ctx* c, const vtq_weight* w, const float* x, in
     t.cnt[q] = reinterpret_cast<unsigned*>(g->peer[q]);
   }
   t.done = reinterpret_cast<unsigned*>(g->base + 8);
+  t.my_cnt = reinterpret_cast<unsigned*>(g->base);
+  t.expected = reinterpret_cast<unsigned*>(g->base + 4);
+  t.wait_signals = wait_signals;
   VTQ_CUDA(c, launch_kq_matvec(m, x, m.in_feat, batch, nullptr, 0,
                                reinterpret_cast<unsigned*>(c->io), c->stream, &t));
   return VTQ_OK;
+}
+
+vtq_status vtq_linear_gather(vtq_ctx* c, const vtq_weight* w, const float* x, int64_t batch,
+                             vtq_gather* g, int64_t y_offset, int64_t ldy, int64_t row0,
+                             uint32_t flags) {
+  return vtq_linear_gather_wait(c, w, x, batch, g, y_offset, ldy, row0, flags, 0);
 }
 
 vtq_status vtq_gather_wait(vtq_ctx* c, vtq_gather* g, uint32_t signals) {

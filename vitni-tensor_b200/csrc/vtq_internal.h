@@ -43,6 +43,12 @@ struct GatherTarget {
   float* y[kMaxRanks];
   unsigned* cnt[kMaxRanks];
   unsigned* done;
+  // wait_signals > 0: the launch's last CTA also waits until this rank's
+  // counter (my_cnt) has `wait_signals` more arrivals than *expected, then
+  // advances *expected, so the launch ends with the whole y gathered.
+  unsigned* my_cnt;
+  unsigned* expected;
+  unsigned wait_signals;
 };
 
 // Transform applied to a batch-1 activation row while the matvec quantises it

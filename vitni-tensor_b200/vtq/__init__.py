@@ -39,7 +39,7 @@ EXPORTS = (
     "vtq_decode_config", "vtq_decode_run", "vtq_decode_close", "vtq_expf", "vtq_sinf",
     "vtq_cosf", "vtq_powf", "vtq_libm_sweep", "vtq_linear_host_noalloc",
     "vtq_gather_create", "vtq_gather_connect", "vtq_gather_y", "vtq_linear_gather",
-    "vtq_gather_wait", "vtq_gather_destroy", "vtq_libm_sweep_device",
+    "vtq_gather_wait", "vtq_gather_destroy", "vtq_libm_sweep_device", "vtq_linear_gather_wait",
     "vtq_decode_timing", "vtq_decode_debug_buffer",
 )
 
@@ -139,6 +139,8 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         "vtq_gather_wait": (c_i32, [c_p, c_p, c_u32]),
         "vtq_gather_destroy": (c_i32, [c_p]),
         "vtq_libm_sweep_device": (c_i32, [c_p, c_sz, c_p]),
+        "vtq_linear_gather_wait": (c_i32, [c_p, c_p, c_p, c_i64, c_p, c_i64, c_i64, c_i64, c_u32,
+                                           c_u32]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -312,9 +314,12 @@ class Gather:
         self.y_floats = y_floats
 
     def linear(self, w: "Weight", x_ptr: int, row0: int, ldy: int, y_offset: int = 0,
-               batch: int = 1):
-        self.ctx._check(self.lib.vtq_linear_gather(self.ctx.handle, w.handle, x_ptr, batch,
-                                                   self.handle, y_offset, ldy, row0, 0))
+               batch: int = 1, wait_signals: int = 0):
+        """wait_signals > 0: the launch ends only once that many rank arrivals
+        (including this launch's) have reached this rank."""
+        self.ctx._check(self.lib.vtq_linear_gather_wait(self.ctx.handle, w.handle, x_ptr, batch,
+                                                        self.handle, y_offset, ldy, row0, 0,
+                                                        wait_signals))
 
     def wait(self, signals: int):
         self.ctx._check(self.lib.vtq_gather_wait(self.ctx.handle, self.handle, signals))
