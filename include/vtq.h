@@ -167,7 +167,25 @@ vtq_status vtq_decode_timing(const vtq_decode* d, float* ms2);
 /* Diagnostic: copy an activation buffer left by the last step (0 x, 1 xb, 2 q,
  * 3 k, 4 v, 5 xo, 6 xb2, 7 gate, 8 up, 9 SwiGLU, 10 logits); n elements. */
 vtq_status vtq_decode_debug_buffer(vtq_decode* d, int which, float* out, size_t n);
+/* How a step runs: 0 a graph of per-op kernels, 1 the same graph with the fused
+ * norm / projection kernels, 2 one persistent cooperative kernel per step.
+ * Environment at open: VTQ_DECODE_PERSISTENT=1 (the persistent kernel, when
+ * the model fits it), VTQ_DECODE_UNFUSED (per-op kernels without the fused
+ * norm). No reference counterpart. */
+int vtq_decode_step_kind(const vtq_decode* d);
 vtq_status vtq_decode_close(vtq_decode* d);
+
+/* ---- The left-to-right fp32 sum of non-negative terms (the sum of squares of
+ * rms_norm_slice, src/ops/rms_norm.rs:97-100) as a CTA computes it: runs of
+ * steps inside one ulp range composed by a parallel scan, crossing steps added
+ * in order by one thread, every run verified (else the plain loop). Test
+ * entry points; no reference counterpart. ---- */
+/* The plan evaluated on the host, step by step; *fallback = 1 when it fell
+ * back to the plain loop. */
+float vtq_exact_sum_host(const float* a, size_t n, int* fallback);
+/* nvec vectors of n terms from host memory, one CTA of nthr threads each
+ * (nthr a multiple of 32, at most 1024); out receives nvec sums. */
+vtq_status vtq_exact_sum_device(const float* host, int nvec, int n, int nthr, float* out);
 
 /* ---- Software transcendentals shared by host and device. ----
  * Bit-for-bit the single-precision functions of the Rust `libm` crate the

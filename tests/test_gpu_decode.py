@@ -14,8 +14,24 @@ SMALL = dict(dim=256, hidden=512, layers=2, heads=4, kv_heads=2, vocab=300, seq_
              rope_theta=10000.0, rms_eps=1e-5)
 
 
-def run_both(blob, prompt, n_new):
+STEP_PATHS = {"graph": ({}, 1), "persistent": ({"VTQ_DECODE_PERSISTENT": "1"}, 2),
+              "unfused": ({"VTQ_DECODE_UNFUSED": "1"}, 0)}
+
+
+@pytest.fixture(params=list(STEP_PATHS))
+def step_path(request, monkeypatch):
+    env, kind = STEP_PATHS[request.param]
+    for k in ("VTQ_DECODE_PERSISTENT", "VTQ_DECODE_UNFUSED"):
+        monkeypatch.delenv(k, raising=False)
+    for k, v in env.items():
+        monkeypatch.setenv(k, v)
+    return kind
+
+
+def run_both(blob, prompt, n_new, kind=None):
     sess = vtq.DecodeSession(blob)
+    if kind is not None:
+        assert sess.step_kind == kind, (sess.step_kind, kind)
     got, lg = sess.run(prompt, n_new, logits=True)
     again, _ = sess.run(prompt, n_new)  # a second run (graph without the logits log)
     sess.close()
@@ -29,7 +45,7 @@ def assert_bits(a, b):
 
 
 @pytest.mark.parametrize("variant", ["q4k_embd", "q6k_embd", "shared_head", "mha"])
-def test_small_models_bit_exact(variant):
+def test_small_models_bit_exact(variant, step_path):
     cfg = dict(SMALL)
     kw = {}
     if variant == "q6k_embd":
@@ -40,16 +56,16 @@ def test_small_models_bit_exact(variant):
         cfg.update(kv_heads=4, hidden=768, layers=3)
     blob = gguf.synthetic_llama(cfg, seed=3, **kw)
     prompt = gguf.prompt_tokens(7, cfg["vocab"], seed=1)
-    got, lg, again, ref, rlg = run_both(blob, prompt, 9)
+    got, lg, again, ref, rlg = run_both(blob, prompt, 9, step_path)
     assert_bits(lg, rlg)
     assert got == ref and again == ref
 
 
-def test_tinyllama_config4_receipt():
+def test_tinyllama_config4_receipt(step_path):
     cfg = gguf.TINYLLAMA
     blob = gguf.synthetic_llama(cfg)
     prompt = gguf.prompt_tokens(16, cfg["vocab"])
-    got, lg, again, ref, rlg = run_both(blob, prompt, 64)
+    got, lg, again, ref, rlg = run_both(blob, prompt, 64, step_path)
     assert_bits(lg, rlg)
     assert got == ref == again
     arch = gguf.arch_string(cfg)

@@ -27,6 +27,9 @@
 #include "vtq_device.cuh"
 #include "vtq_internal.h"
 #include "vtq_libm.h"
+#include "decode_ops.cuh"
+#include "exact_sum.cuh"
+#include "decode_mk.h"
 
 namespace vtq {
 
@@ -213,68 +216,24 @@ Gguf parse_gguf(const uint8_t* blob, size_t len) {
 
 // ------------------------------------------------------------- kernels ----
 
-constexpr uint32_t FULL = 0xffffffffu;
 
-struct StepState {  // device-resident per-run state
-  int pos;          // position of the step about to run
-  uint32_t cur;     // token fed at `pos`
-  int n_prompt, total, n_gen;
-};
 
 // embedding_row (forward_quantized.rs:818-919): dequantise one row of the
 // table into x. Device layouts as uploaded (Q6_K regrouped, see repack.cu).
 __global__ void embed_kernel(const uint8_t* table, int dtype, int64_t pitch, int dim,
                              const StepState* st, float* x) {
   const uint32_t row = st->cur;
-  const uint8_t* r = table + (int64_t)row * pitch;
-  for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < dim; e += gridDim.x * blockDim.x) {
-    float v;
-    if (dtype == T_F32) {
-      v = reinterpret_cast<const float*>(r)[e];
-    } else if (dtype == T_Q8_0) {
-      const uint8_t* b = r + (e >> 5) * 34;
-      v = __fmul_rn(f16_bits_to_f32(b[0] | (b[1] << 8)), (float)(int8_t)b[2 + (e & 31)]);
-    } else if (dtype == T_Q4_K) {  // quant.rs:280-326
-      const uint8_t* sb = r + (e >> 8) * 144;
-      const int k = e & 255, half = k >> 6, hi = (k >> 5) & 1, l = k & 31, j = 2 * half + hi;
-      const uint8_t* s = sb + 4;
-      int sc, m;
-      if (j < 4) {
-        sc = s[j] & 63;
-        m = s[j + 4] & 63;
-      } else {
-        sc = (s[j + 4] & 0x0F) | ((s[j - 4] >> 6) << 4);
-        m = (s[j + 4] >> 4) | ((s[j] >> 6) << 4);
-      }
-      const float d = f16_bits_to_f32(sb[0] | (sb[1] << 8));
-      const float dmin = f16_bits_to_f32(sb[2] | (sb[3] << 8));
-      const uint8_t byte = sb[16 + 32 * half + l];
-      const int q = hi ? (byte >> 4) : (byte & 15);
-      v = __fsub_rn(__fmul_rn(__fmul_rn(d, (float)sc), (float)q), __fmul_rn(dmin, (float)m));
-    } else {  // Q6_K, device layout: group of G superblocks
-      const int s = e >> 8, gi = s >> 3, i = s & 7;
-      const int S = dim >> 8, G = min(8, S - 8 * gi);
-      const uint8_t* gb = r + gi * 1680;
-      const int k = e & 255, half = k >> 7, w = k & 127, t = w >> 5, l = w & 31;
-      // ql byte (64 half + l + 32 (t & 1)), nibble t >> 1; qh byte (32 half + l), bits 2t.
-      const int qlb = 64 * half + l + 32 * (t & 1), qhb = 32 * half + l;
-      const uint8_t ql = gb[16 * (G * (qlb >> 4) + i) + (qlb & 15)];
-      const uint8_t qh = gb[128 * G + 16 * (G * (qhb >> 4) + i) + (qhb & 15)];
-      const int q = (int)(((t >> 1) ? (ql >> 4) : (ql & 15)) | (((qh >> (2 * t)) & 3) << 4)) - 32;
-      const int sc = (int8_t)gb[192 * G + 16 * i + 8 * half + (l >> 4) + 2 * t];
-      const float d = f16_bits_to_f32(gb[208 * G + 2 * i] | (gb[208 * G + 2 * i + 1] << 8));
-      v = __fmul_rn(__fmul_rn(d, (float)sc), (float)q);  // d * s * q (quant.rs:378-381)
-    }
-    x[e] = v;
-  }
+  for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < dim; e += gridDim.x * blockDim.x)
+    x[e] = embed_value(table, dtype, pitch, dim, row, e);
 }
 
 // x = x + delta (if delta), then xb = rms_norm(x) * w (rms_norm.rs:94-108):
-// sumsq accumulated serially in element order by one thread.
+// sumsq is the left-to-right fp32 sum (exact_serial_sum computes it with the CTA).
 __global__ void __launch_bounds__(256) rmsnorm_kernel(float* x, const float* delta, const float* w, float eps, int n,
                                float* out) {
   extern __shared__ float sq[];
   __shared__ float s_scale;
+  __shared__ xsum::Scratch scr;
   pdl_wait();
   pdl_release();
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
@@ -286,8 +245,9 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(float* x, const float* del
     sq[i] = __fmul_rn(v, v);
   }
   __syncthreads();
+  const float s = xsum::exact_serial_sum<16>(sq, n, &scr, threadIdx.x, blockDim.x,
+                                         [] { __syncthreads(); });  // rms_norm.rs:97-100
   if (threadIdx.x == 0) {
-    const float s = serial_sum(sq, n);  // rms_norm.rs:97-100
     const float mean = __fdiv_rn(s, (float)n);
     s_scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
   }
@@ -306,6 +266,7 @@ __global__ void __launch_bounds__(256) rmsnorm_res_kernel(const float* x, const 
                                                           float* out, float* res) {
   extern __shared__ float sq[];
   __shared__ float s_scale;
+  __shared__ xsum::Scratch scr;
   pdl_wait();
   pdl_release();
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
@@ -315,8 +276,9 @@ __global__ void __launch_bounds__(256) rmsnorm_res_kernel(const float* x, const 
     sq[i] = __fmul_rn(v, v);
   }
   __syncthreads();
+  const float s = xsum::exact_serial_sum<16>(sq, n, &scr, threadIdx.x, blockDim.x,
+                                         [] { __syncthreads(); });  // rms_norm.rs:97-100
   if (threadIdx.x == 0) {
-    const float s = serial_sum(sq, n);
     const float mean = __fdiv_rn(s, (float)n);
     s_scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
   }
@@ -326,115 +288,17 @@ __global__ void __launch_bounds__(256) rmsnorm_res_kernel(const float* x, const 
     out[i] = __fmul_rn(__fmul_rn(res[i], scale), w[i]);
 }
 
-// Attention for one query head with the step's RoPE fused in
-// (forward_quantized.rs:407-500): rotate this head's q and its kv head's new
-// k (interleaved pairs, host cos/sin tables), store the rotated k and the raw
-// v at `pos` of the cache (first query head of each kv group), then serial
-// scores over head_dim, softmax with a serial sum, and a serial P.V sum over
-// positions for every head dimension. Positions < pos come from the cache;
-// position pos uses the k/v computed here (the same values the cache gets).
+// One query head per CTA (attention_head, decode_ops.cuh).
 __global__ void attention_rope_kernel(const float* q, const float* k, const float* v, float* kc,
                                       float* vc, int layer, int seq_len, int kv_dim, int hs,
                                       int kv_mul, const float* rcos, const float* rsin,
                                       const StepState* st, float* out) {
   extern __shared__ float sm[];
-  float* qh = sm;            // [hs] rotated query head
-  float* kh = sm + hs;       // [hs] rotated new key
-  float* vh = sm + 2 * hs;   // [hs] new value
-  float* att = sm + 3 * hs;  // [pos + 1]
-  __shared__ float s_max, s_inv;
+  __shared__ float red[2];
   pdl_wait();
   pdl_release();
-  const int h = blockIdx.x, g = h / kv_mul, pos = st->pos, np = pos + 1;
-  const size_t off = ((size_t)layer * seq_len + pos) * kv_dim;
-  for (int p = threadIdx.x; p < hs / 2; p += blockDim.x) {
-    const float fcr = rcos[(size_t)pos * (hs / 2) + p], fci = rsin[(size_t)pos * (hs / 2) + p];
-    const float q0 = q[h * hs + 2 * p], q1 = q[h * hs + 2 * p + 1];
-    qh[2 * p] = __fsub_rn(__fmul_rn(q0, fcr), __fmul_rn(q1, fci));
-    qh[2 * p + 1] = __fadd_rn(__fmul_rn(q0, fci), __fmul_rn(q1, fcr));
-    const float k0 = k[g * hs + 2 * p], k1 = k[g * hs + 2 * p + 1];
-    const float r0 = __fsub_rn(__fmul_rn(k0, fcr), __fmul_rn(k1, fci));
-    const float r1 = __fadd_rn(__fmul_rn(k0, fci), __fmul_rn(k1, fcr));
-    kh[2 * p] = r0;
-    kh[2 * p + 1] = r1;
-    vh[2 * p] = v[g * hs + 2 * p];
-    vh[2 * p + 1] = v[g * hs + 2 * p + 1];
-    if (h % kv_mul == 0) {
-      kc[off + g * hs + 2 * p] = r0;
-      kc[off + g * hs + 2 * p + 1] = r1;
-      vc[off + g * hs + 2 * p] = vh[2 * p];
-      vc[off + g * hs + 2 * p + 1] = vh[2 * p + 1];
-    }
-  }
-  __syncthreads();
-  const float* kbase = kc + (size_t)layer * seq_len * kv_dim + g * hs;
-  const float* vbase = vc + (size_t)layer * seq_len * kv_dim + g * hs;
-  const float root = __fsqrt_rn((float)hs);
-  for (int t = threadIdx.x; t < np; t += blockDim.x) {
-    const float* kt = (t == pos) ? kh : kbase + (size_t)t * kv_dim;
-    float score = 0.0f;
-    if ((hs & 15) == 0) {
-      for (int d0 = 0; d0 < hs; d0 += 16) {
-        float4 kv4[4], qv4[4];
-#pragma unroll
-        for (int u = 0; u < 4; u++) {
-          kv4[u] = *reinterpret_cast<const float4*>(kt + d0 + 4 * u);
-          qv4[u] = *reinterpret_cast<const float4*>(qh + d0 + 4 * u);
-        }
-#pragma unroll
-        for (int u = 0; u < 4; u++) {
-          score = __fadd_rn(score, __fmul_rn(qv4[u].x, kv4[u].x));
-          score = __fadd_rn(score, __fmul_rn(qv4[u].y, kv4[u].y));
-          score = __fadd_rn(score, __fmul_rn(qv4[u].z, kv4[u].z));
-          score = __fadd_rn(score, __fmul_rn(qv4[u].w, kv4[u].w));
-        }
-      }
-    } else {
-      for (int d = 0; d < hs; d++) score = __fadd_rn(score, __fmul_rn(qh[d], kt[d]));
-    }
-    att[t] = __fdiv_rn(score, root);
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    float mx = -INFINITY;
-    for (int t = 0; t < np; t++)
-      if (att[t] > mx) mx = att[t];
-    s_max = mx;
-  }
-  __syncthreads();
-  for (int t = threadIdx.x; t < np; t += blockDim.x) att[t] = libm::expf(__fsub_rn(att[t], s_max));
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    float sum = 0.0f;
-    int t = 0;
-    for (; t + 4 <= np; t += 4) {
-      const float a0 = att[t], a1 = att[t + 1], a2 = att[t + 2], a3 = att[t + 3];
-      sum = __fadd_rn(sum, a0);
-      sum = __fadd_rn(sum, a1);
-      sum = __fadd_rn(sum, a2);
-      sum = __fadd_rn(sum, a3);
-    }
-    for (; t < np; t++) sum = __fadd_rn(sum, att[t]);
-    s_inv = __fdiv_rn(1.0f, sum);
-  }
-  __syncthreads();
-  for (int t = threadIdx.x; t < np; t += blockDim.x) att[t] = __fmul_rn(att[t], s_inv);
-  __syncthreads();
-  for (int d = threadIdx.x; d < hs; d += blockDim.x) {
-    float acc = 0.0f;
-    int t = 0;
-    for (; t + 4 <= pos; t += 4) {
-      const float v0 = vbase[(size_t)t * kv_dim + d], v1 = vbase[(size_t)(t + 1) * kv_dim + d];
-      const float v2 = vbase[(size_t)(t + 2) * kv_dim + d], v3 = vbase[(size_t)(t + 3) * kv_dim + d];
-      acc = __fadd_rn(acc, __fmul_rn(att[t], v0));
-      acc = __fadd_rn(acc, __fmul_rn(att[t + 1], v1));
-      acc = __fadd_rn(acc, __fmul_rn(att[t + 2], v2));
-      acc = __fadd_rn(acc, __fmul_rn(att[t + 3], v3));
-    }
-    for (; t < pos; t++) acc = __fadd_rn(acc, __fmul_rn(att[t], vbase[(size_t)t * kv_dim + d]));
-    acc = __fadd_rn(acc, __fmul_rn(att[pos], vh[d]));
-    out[h * hs + d] = acc;
-  }
+  attention_head(blockIdx.x, q, k, v, kc, vc, layer, seq_len, kv_dim, hs, kv_mul, rcos, rsin,
+                 st->pos, out, sm, red, threadIdx.x, blockDim.x, [] { __syncthreads(); });
 }
 
 // SwiGLU: silu(g) * up with silu = g / (1 + expf(-g)) (forward_quantized.rs:556-561).
@@ -448,52 +312,15 @@ __global__ void swiglu_kernel(const float* g, const float* u, float* out, int n)
   }
 }
 
-// argmax (argmax.rs:49-60: first index of the maximum, strict >) and the
-// token choice of the run loop (inference.rs:318-326), then pos += 1.
+// Next-token choice (argmax_next, decode_ops.cuh) in one CTA.
 __global__ void argmax_next_kernel(const float* logits, int n, StepState* st,
                                    const uint32_t* prompt, uint32_t* out_tokens) {
   __shared__ float bv[32];
   __shared__ int bi[32];
   pdl_wait();
   pdl_release();
-  float best = -INFINITY;
-  int besti = 0x7fffffff;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    const float v = logits[i];
-    if (v > best || (v == best && i < besti)) {
-      best = v;
-      besti = i;
-    }
-  }
-  for (int o = 16; o; o >>= 1) {
-    const float ov = __shfl_down_sync(FULL, best, o);
-    const int oi = __shfl_down_sync(FULL, besti, o);
-    if (ov > best || (ov == best && oi < besti)) {
-      best = ov;
-      besti = oi;
-    }
-  }
-  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (lane == 0) {
-    bv[w] = best;
-    bi[w] = besti;
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    for (int k = 1; k < (int)(blockDim.x >> 5); k++)
-      if (bv[k] > best || (bv[k] == best && bi[k] < besti)) {
-        best = bv[k];
-        besti = bi[k];
-      }
-    // NaN at index 0 is never beaten by a strict > (sequential rule).
-    if (logits[0] != logits[0] || besti == 0x7fffffff) besti = 0;
-    const int pos = st->pos;
-    const uint32_t picked = (uint32_t)besti;
-    const uint32_t next = (pos + 1 < st->n_prompt) ? prompt[pos + 1] : picked;
-    if (pos >= st->n_prompt) out_tokens[st->n_gen++] = next;
-    st->cur = next;
-    st->pos = pos + 1;
-  }
+  argmax_next(logits, n, st, prompt, out_tokens, bv, bi, threadIdx.x, blockDim.x,
+              [] { __syncthreads(); });
 }
 
 // Copy the step's logits into the per-position log (optional output).
@@ -534,6 +361,7 @@ struct vtq_decode {
   float* xr = nullptr;  // second residual buffer (fused path: the norms alternate x <-> xr)
   bool fused = false;   // every linear integer k-quant: norms/SwiGLU fused into the matvecs
   int fuse_mask = 2;    // 1: attention norm, 2: FFN norm, 4: SwiGLU into the matvecs (2 measured fastest)
+  MkPlan* mk = nullptr;  // persistent one-kernel step (decode_mk.cu), when the model fits
   float* logit_log = nullptr;
   size_t logit_log_cap = 0;
   StepState* st = nullptr;
@@ -939,10 +767,50 @@ vtq_status vtq_decode_open(vtq_ctx* ctx, int device, const uint8_t* gguf, size_t
   for (auto& L : d->layers)
     d->fused = d->fused && L.fused_qk && L.fused_13 && kq(L.wqk) && kq(L.wv) && kq(L.wo) &&
                kq(L.w13) && kq(L.w2);
+  if (d->fused) {
+    MkModel mm;
+    mm.dim = dim;
+    mm.hidden = d->hidden;
+    mm.n_layers = d->n_layers;
+    mm.n_heads = d->n_heads;
+    mm.n_kv_heads = d->n_kv_heads;
+    mm.vocab = d->vocab;
+    mm.seq_len = d->seq_len;
+    mm.eps = d->rms_eps;
+    mm.embd = d->embd;
+    mm.head = d->head;
+    mm.rms_final = d->rms_final;
+    for (auto& L : d->layers) mm.layers.push_back({L.wqk, L.wv, L.wo, L.w13, L.w2, L.rms_att, L.rms_ffn});
+    mm.x = d->x;
+    mm.xr = d->xr;
+    mm.q = d->q;
+    mm.v = d->v;
+    mm.xo = d->xo;
+    mm.xb2 = d->xb2;
+    mm.g = d->g;
+    mm.logits = d->logits;
+    mm.kc = d->kc;
+    mm.vc = d->vc;
+    mm.rcos = d->rcos;
+    mm.rsin = d->rsin;
+    mm.st = d->st;
+    mm.prompt = d->prompt;
+    mm.out_tokens = d->out_tokens;
+    mm.status = d->status;
+    if (mk_supported(mm) && mk_build(mm, &d->mk) != cudaSuccess) {
+      d->mk = nullptr;
+      cudaGetLastError();  // fall back to the per-op graph
+    }
+  }
   return VTQ_OK;
 }
 
 const char* vtq_decode_last_error(const vtq_decode* d) { return d ? d->err.c_str() : "null"; }
+
+int vtq_decode_step_kind(const vtq_decode* d) {
+  if (!d) return -1;
+  return d->mk ? 2 : d->fused ? 1 : 0;
+}
 
 vtq_status vtq_decode_config(const vtq_decode* d, int64_t* out8) {
   if (!d || !out8) return VTQ_ERR_INVALID_ARG;
@@ -974,6 +842,33 @@ vtq_status vtq_decode_run(vtq_decode* d, const uint32_t* prompt, size_t n_prompt
       cudaGraphExecDestroy(d->graph);
       d->graph = nullptr;
     }
+  }
+  if (d->mk) {
+    // Persistent step kernel: one cooperative launch per position.
+    if (!d->ev[0])
+      for (auto& e : d->ev) DCUDA(d, cudaEventCreate(&e));
+    DCUDA(d, cudaEventRecord(d->ev[0], d->stream));
+    StepState hs0{0, prompt[0], (int)n_prompt, (int)total, 0};
+    DCUDA(d, cudaMemcpyAsync(d->st, &hs0, sizeof hs0, cudaMemcpyHostToDevice, d->stream));
+    DCUDA(d, cudaMemcpyAsync(d->prompt, prompt, n_prompt * 4, cudaMemcpyHostToDevice, d->stream));
+    DCUDA(d, cudaEventRecord(d->ev[1], d->stream));
+    for (size_t pos = 0; pos < total; pos++)
+      DCUDA(d, mk_launch(d->mk, want_logits ? d->logit_log : nullptr, d->stream));
+    DCUDA(d, cudaEventRecord(d->ev[2], d->stream));
+    if (n_new)
+      DCUDA(d, cudaMemcpyAsync(out_tokens, d->out_tokens, n_new * 4, cudaMemcpyDeviceToHost,
+                               d->stream));
+    if (want_logits)
+      DCUDA(d, cudaMemcpyAsync(logits, d->logit_log, total * d->vocab * 4,
+                               cudaMemcpyDeviceToHost, d->stream));
+    unsigned stat = 0;
+    DCUDA(d, cudaMemcpyAsync(&stat, d->status, 4, cudaMemcpyDeviceToHost, d->stream));
+    DCUDA(d, cudaEventRecord(d->ev[3], d->stream));
+    DCUDA(d, cudaStreamSynchronize(d->stream));
+    DCUDA(d, cudaEventElapsedTime(&d->ms_steps, d->ev[1], d->ev[2]));
+    DCUDA(d, cudaEventElapsedTime(&d->ms_call, d->ev[0], d->ev[3]));
+    if (stat) return dfail(d, VTQ_ERR_TIMEOUT, "decode: a device-side wait timed out");
+    return VTQ_OK;
   }
   if (!d->graph || d->graph_logs != want_logits) {
     if (d->graph) cudaGraphExecDestroy(d->graph);
@@ -1047,6 +942,7 @@ vtq_status vtq_decode_close(vtq_decode* d) {
   for (auto e : d->ev)
     if (e) cudaEventDestroy(e);
   if (d->side) cudaStreamSynchronize(d->side);
+  mk_free(d->mk);
   if (d->fork) cudaEventDestroy(d->fork);
   if (d->join) cudaEventDestroy(d->join);
   for (void* p : d->allocs) cudaFree(p);

@@ -40,7 +40,8 @@ EXPORTS = (
     "vtq_cosf", "vtq_powf", "vtq_libm_sweep", "vtq_linear_host_noalloc",
     "vtq_gather_create", "vtq_gather_connect", "vtq_gather_y", "vtq_linear_gather",
     "vtq_gather_wait", "vtq_gather_destroy", "vtq_libm_sweep_device", "vtq_linear_gather_wait",
-    "vtq_decode_timing", "vtq_decode_debug_buffer",
+    "vtq_decode_timing", "vtq_decode_debug_buffer", "vtq_decode_step_kind",
+    "vtq_exact_sum_host", "vtq_exact_sum_device",
 )
 
 
@@ -130,6 +131,9 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         "vtq_powf": (ctypes.c_float, [ctypes.c_float, ctypes.c_float]),
         "vtq_libm_sweep": (None, [c_p, c_sz, c_p]),
         "vtq_decode_timing": (c_i32, [c_p, c_p]),
+        "vtq_decode_step_kind": (c_i32, [c_p]),
+        "vtq_exact_sum_host": (ctypes.c_float, [c_p, c_sz, c_p]),
+        "vtq_exact_sum_device": (c_i32, [c_p, c_i32, c_i32, c_i32, c_p]),
         "vtq_decode_debug_buffer": (c_i32, [c_p, ctypes.c_int, c_p, c_sz]),
         "vtq_linear_host_noalloc": (c_i32, [c_i32, c_p, c_i64, c_i64, c_p, c_p, c_i64, c_p]),
         "vtq_gather_create": (c_i32, [c_p, c_i32, c_i32, c_sz, ctypes.POINTER(c_p), c_p]),
@@ -349,6 +353,8 @@ class DecodeSession:
         self.lib.vtq_decode_config(self.handle, _ptr(cfg))
         keys = ("dim", "hidden", "layers", "heads", "kv_heads", "vocab", "seq_len", "shared")
         self.config = {k: int(v) for k, v in zip(keys, cfg)}
+        # 0 per-op graph, 1 fused-op graph, 2 persistent kernel per step
+        self.step_kind = int(self.lib.vtq_decode_step_kind(self.handle))
 
     def run(self, prompt, n_new: int, logits: bool = False):
         """Returns (generated token ids, per-step logits [n_prompt + n_new, vocab] or None)."""
@@ -377,6 +383,25 @@ class DecodeSession:
             self.close()
         except Exception:
             pass
+
+
+def exact_sum_host(a) -> tuple:
+    """(left-to-right fp32 sum of a, fell back to the plain loop) through the
+    host evaluation of the run/crossing plan."""
+    a = _as_f32(a)
+    fb = ctypes.c_int(0)
+    s = load_library().vtq_exact_sum_host(_ptr(a), a.size, ctypes.byref(fb))
+    return np.float32(s), bool(fb.value)
+
+
+def exact_sum_device(vecs, nthr: int = 256) -> np.ndarray:
+    """Sums of the rows of vecs [nvec, n], one CTA of nthr threads per row."""
+    v = np.ascontiguousarray(vecs, dtype=np.float32)
+    out = np.zeros(v.shape[0], np.float32)
+    st = load_library().vtq_exact_sum_device(_ptr(v), v.shape[0], v.shape[1], nthr, _ptr(out))
+    if st != OK:
+        raise _ERRORS.get(st, Error)(f"vtq_exact_sum_device: status {st}")
+    return out
 
 
 def device_layout_bytes(dtype: int, in_feat: int, rows: int) -> int:
