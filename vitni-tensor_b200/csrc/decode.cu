@@ -302,13 +302,14 @@ __global__ void attention_rope_kernel(const float* q, const float* k, const floa
 }
 
 // SwiGLU: silu(g) * up with silu = g / (1 + expf(-g)) (forward_quantized.rs:556-561).
-__global__ void swiglu_kernel(const float* g, const float* u, float* out, int n) {
+// g and u are read with stride `st` (2 for the interleaved gate|up output).
+__global__ void swiglu_kernel(const float* g, const float* u, int st, float* out, int n) {
   pdl_wait();
   pdl_release();
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
-    const float gi = g[i];
+    const float gi = g[(int64_t)i * st];
     const float silu = __fdiv_rn(gi, __fadd_rn(1.0f, libm::expf(-gi)));
-    out[i] = __fmul_rn(silu, u[i]);
+    out[i] = __fmul_rn(silu, u[(int64_t)i * st]);
   }
 }
 
@@ -360,7 +361,7 @@ struct vtq_decode {
   float *x, *xb, *q, *k, *v, *xo, *xb2, *g, *u, *inner, *logits;
   float* xr = nullptr;  // second residual buffer (fused path: the norms alternate x <-> xr)
   bool fused = false;   // every linear integer k-quant: norms/SwiGLU fused into the matvecs
-  int fuse_mask = 2;    // 1: attention norm, 2: FFN norm, 4: SwiGLU into the matvecs (2 measured fastest)
+  int fuse_mask = 2;    // RMSNorm into the consuming matvec: 1 attention, 2 FFN (2 measured fastest)
   MkPlan* mk = nullptr;  // persistent one-kernel step (decode_mk.cu), when the model fits
   float* logit_log = nullptr;
   size_t logit_log_cap = 0;
@@ -479,7 +480,7 @@ vtq_status enqueue_step(vtq_decode* d, bool log_logits) {
   if (d->fused) {
     // RMSNorm runs inside the matvecs that consume it (every CTA computes the
     // serial sum while its weights stream in; CTA 0 of one launch stores the
-    // residual into the other buffer) and SwiGLU inside the down projection.
+    // residual into the other buffer) and SwiGLU in the gate|up epilogue.
     auto mv = [&](const DevMatrix& m, const float* x, float* y, cudaStream_t st,
                   const KqXform* xf) {
       return launch_kq_matvec(m, x, m.in_feat, 1, y, m.out_feat, d->status, st, nullptr, xf);
@@ -522,22 +523,16 @@ vtq_status enqueue_step(vtq_decode* d, bool log_logits) {
         ffn.nw = L.rms_ffn;
         ffn.eps = d->rms_eps;
         ffn.res_out = d->x;
-        DCUDA(d, mv(L.w13, d->xr, d->g, s, &ffn));
+        ffn.swiglu_pairs = 1;
+        DCUDA(d, mv(L.w13, d->xr, d->inner, s, &ffn));
       } else {
         DCUDA(d, launch_pdl(rmsnorm_res_kernel, 1, 256, rms_smem, s, d->xr, d->xb2, L.rms_ffn,
                             d->rms_eps, dim, d->xb, d->x));
-        DCUDA(d, mv(L.w13, d->xb, d->g, s, nullptr));
-      }
-      if (fz & 4) {
         KqXform sw;
-        sw.kind = 1;
-        sw.x2 = d->u;
-        DCUDA(d, mv(L.w2, d->g, d->xb2, s, &sw));
-      } else {
-        DCUDA(d, launch_pdl(swiglu_kernel, (d->hidden + 255) / 256, 256, 0, s, d->g, d->u,
-                            d->inner, d->hidden));
-        DCUDA(d, mv(L.w2, d->inner, d->xb2, s, nullptr));
+        sw.swiglu_pairs = 1;
+        DCUDA(d, mv(L.w13, d->xb, d->inner, s, &sw));
       }
+      DCUDA(d, mv(L.w2, d->inner, d->xb2, s, nullptr));
       delta = d->xb2;
     }
     KqXform fin;
@@ -583,8 +578,9 @@ vtq_status enqueue_step(vtq_decode* d, bool log_logits) {
       DCUDA(d, launch_kq_or_canon(L.w1, d->xb, d->g, d->status, s));
       DCUDA(d, launch_kq_or_canon(L.w3, d->xb, d->u, d->status, s));
     }
-    DCUDA(d, launch_pdl(swiglu_kernel, (d->hidden + 255) / 256, 256, 0, s, d->g, d->u, d->inner,
-                        d->hidden));
+    // The fused gate|up output is interleaved (gate_i, up_i).
+    DCUDA(d, launch_pdl(swiglu_kernel, (d->hidden + 255) / 256, 256, 0, s, d->g,
+                        L.fused_13 ? d->g + 1 : d->u, L.fused_13 ? 2 : 1, d->inner, d->hidden));
     DCUDA(d, launch_kq_or_canon(L.w2, d->inner, d->xb2, d->status, s));
     delta = d->xb2;
   }
@@ -693,22 +689,39 @@ vtq_status vtq_decode_open(vtq_ctx* ctx, int device, const uint8_t* gguf, size_t
     const GTensor* t1 = need(d, g, p + "ffn_gate.weight");
     const GTensor* t3 = need(d, g, p + "ffn_up.weight");
     if (!tq || !tk || !t1 || !t3) return VTQ_ERR_INTERNAL;
+    // interleave: rows (a_0, b_0, a_1, b_1, ...) for the gate|up pair epilogue
+    // (ma / mb then do not describe separate matrices and stay unused).
     auto fuse = [&](const GTensor* ta, const GTensor* tb, int64_t in, int64_t ra, int64_t rb,
-                    DevMatrix* ma, DevMatrix* mb, DevMatrix* both, bool* fused) -> vtq_status {
+                    DevMatrix* ma, DevMatrix* mb, DevMatrix* both, bool* fused,
+                    bool interleave) -> vtq_status {
       if (ta->dtype != tb->dtype || (ta->dtype != T_Q4_K && ta->dtype != T_Q6_K)) return VTQ_OK;
       const int64_t pitch = device_pitch(ta->dtype, in);
-      if (pitch <= 0) return VTQ_OK;
+      if (pitch <= 0 || (interleave && ra != rb)) return VTQ_OK;
       uint8_t* buf;
       if (vtq_status e = dalloc(d, &buf, (size_t)((ra + rb) * pitch + 16))) return e;
-      if (vtq_status e = upload_matrix(d, *ta, in, ra, ma, buf)) return e;
-      if (vtq_status e = upload_matrix(d, *tb, in, rb, mb, buf + ra * pitch)) return e;
+      uint8_t* tmp = buf;
+      if (interleave) DCUDA(d, cudaMalloc(&tmp, (size_t)((ra + rb) * pitch + 16)));
+      vtq_status e = upload_matrix(d, *ta, in, ra, ma, tmp);
+      if (!e) e = upload_matrix(d, *tb, in, rb, mb, tmp + ra * pitch);
+      if (!e && interleave) {
+        for (int h = 0; h < 2 && !e; h++)
+          if (cudaMemcpy2D(buf + h * pitch, 2 * pitch, tmp + h * ra * pitch, pitch, pitch, ra,
+                           cudaMemcpyDeviceToDevice) != cudaSuccess)
+            e = dfail(d, VTQ_ERR_GPU, "decode session: interleaving gate|up failed");
+        if (!e && cudaMemset(buf + (ra + rb) * pitch, 0, 16) != cudaSuccess)
+          e = dfail(d, VTQ_ERR_GPU, "decode session: interleaving gate|up failed");
+      }
+      if (interleave) cudaFree(tmp);
+      if (e) return e;
       *both = *ma;
+      both->data = buf;
       both->out_feat = ra + rb;
       *fused = true;
       return VTQ_OK;
     };
-    if ((s = fuse(tq, tk, dim, dim, kv_dim, &L.wq, &L.wk, &L.wqk, &L.fused_qk))) return s;
-    if ((s = fuse(t1, t3, dim, d->hidden, d->hidden, &L.w1, &L.w3, &L.w13, &L.fused_13))) return s;
+    if ((s = fuse(tq, tk, dim, dim, kv_dim, &L.wq, &L.wk, &L.wqk, &L.fused_qk, false))) return s;
+    if ((s = fuse(t1, t3, dim, d->hidden, d->hidden, &L.w1, &L.w3, &L.w13, &L.fused_13, true)))
+      return s;
     for (auto& mm : mats) {
       if ((L.fused_qk && (mm.m == &L.wq || mm.m == &L.wk)) ||
           (L.fused_13 && (mm.m == &L.w1 || mm.m == &L.w3)))
@@ -763,7 +776,7 @@ vtq_status vtq_decode_open(vtq_ctx* ctx, int device, const uint8_t* gguf, size_t
   auto kq = [](const DevMatrix& m) { return m.dtype == T_Q4_K || m.dtype == T_Q6_K; };
   d->fused = kq(d->head) && dim % 256 == 0 && d->hidden % 256 == 0 && dim * 4 <= 65536 &&
              d->hidden * 4 <= 65536 && getenv("VTQ_DECODE_UNFUSED") == nullptr;
-  if (const char* e = getenv("VTQ_DECODE_FUSE")) d->fuse_mask = atoi(e) & 7;
+  if (const char* e = getenv("VTQ_DECODE_FUSE")) d->fuse_mask = atoi(e) & 3;
   for (auto& L : d->layers)
     d->fused = d->fused && L.fused_qk && L.fused_13 && kq(L.wqk) && kq(L.wv) && kq(L.wo) &&
                kq(L.w13) && kq(L.w2);

@@ -62,7 +62,7 @@ struct MkPhase {
   // MATVEC
   KqParams kp;
   int qt;    // 0 Q4_K, 1 Q6_K
-  int xsrc;  // XS_GLOBAL: kp.x (kp.xf.kind 0 or 1), XS_NORMED: the NORM result
+  int xsrc;  // XS_GLOBAL: kp.x, XS_NORMED: the NORM result
   // ATTN
   int layer;
 };
@@ -92,9 +92,12 @@ __device__ __forceinline__ void cons_sync() {
   asm volatile("bar.sync 1, %0;" ::"n"(MK_CW * 32) : "memory");
 }
 
+// This CTA's rows of a MATVEC phase (dealt in (gate, up) pairs for the
+// SwiGLU epilogue).
 __device__ __forceinline__ int mv_rows(const KqParams& p, int bid, int* r0) {
-  *r0 = bid * p.rows_base + min(bid, p.rows_rem);
-  return p.rows_base + (bid < p.rows_rem ? 1 : 0);
+  const int unit = p.epi ? 2 : 1;
+  *r0 = unit * (bid * p.rows_base + min(bid, p.rows_rem));
+  return unit * (p.rows_base + (bid < p.rows_rem ? 1 : 0));
 }
 
 __global__ void __launch_bounds__(MK_THREADS, 1) decode_mk_kernel(const MkArgs a) {
@@ -373,7 +376,7 @@ cudaError_t mk_build(const MkModel& m, MkPlan** out) {
   plan->smem = off_ring + nst * MK_SLOT;
 
   std::vector<MkPhase> ph;
-  auto matvec = [&](const DevMatrix& d, const float* x, float* y, int xsrc, const float* x2,
+  auto matvec = [&](const DevMatrix& d, const float* x, float* y, int xsrc, bool pairs,
                     int barrier) {
     MkPhase P{};
     P.kind = PH_MATVEC;
@@ -393,23 +396,20 @@ cudaError_t mk_build(const MkModel& m, MkPlan** out) {
     p.W = d.data;
     p.pitch = d.pitch;
     p.R = (int)d.out_feat;
-    const int g = (int)std::min<int64_t>(d.out_feat, grid);
-    p.rows_base = p.R / grid;
-    p.rows_rem = p.R % grid;
-    (void)g;
+    p.epi = pairs ? 1 : 0;  // gate|up rows interleaved: y = silu(gate) * up
+    const int unit = pairs ? 2 : 1;
+    p.rows_base = p.R / unit / grid;
+    p.rows_rem = p.R / unit % grid;
     p.y = y;
-    p.ldy = d.out_feat;
+    p.ldy = d.out_feat / unit;
     p.lpr = lpr;
     p.status = m.status;
-    const int rows_per_cta = p.rows_base + (p.rows_rem ? 1 : 0);
+    const int rows_per_cta = unit * (p.rows_base + (p.rows_rem ? 1 : 0));
     int rps = std::max(rpw, (int)(MK_SLOT / d.pitch) / rpw * rpw);
     rps = std::min(rps, std::max(rpw, (rows_per_cta + rpw - 1) / rpw * rpw));
     p.rps = rps;
-    if ((uint32_t)(rps * d.pitch) > MK_SLOT) p.rps = 0;  // rows too long for a slot
-    if (x2) {
-      p.xf.kind = 1;  // SwiGLU of gate (x) and up (x2) while quantising
-      p.xf.x2 = x2;
-    }
+    if ((uint32_t)(rps * d.pitch) > MK_SLOT) p.rps = 0;   // rows too long for a slot
+    if (pairs && (rpw < 2 || p.R % 2)) p.rps = 0;         // a pair must share a warp pass
     ph.push_back(P);
   };
   auto norm = [&](const float* x, const float* delta, const float* nw, float* res) {
@@ -431,25 +431,24 @@ cudaError_t mk_build(const MkModel& m, MkPlan** out) {
   const float* delta = nullptr;
   float* A = m.x;
   float* B = m.xr;
-  float* u = m.g + m.hidden;
   for (int l = 0; l < m.n_layers; l++) {
     const MkLayer& L = m.layers[l];
     norm(A, delta, L.rms_att, B);
-    matvec(L.wqk, nullptr, m.q, XS_NORMED, nullptr, 0);
-    matvec(L.wv, nullptr, m.v, XS_NORMED, nullptr, 1);
+    matvec(L.wqk, nullptr, m.q, XS_NORMED, false, 0);
+    matvec(L.wv, nullptr, m.v, XS_NORMED, false, 1);
     MkPhase At{};
     At.kind = PH_ATTN;
     At.barrier = 1;
     At.layer = l;
     ph.push_back(At);
-    matvec(L.wo, m.xo, m.xb2, XS_GLOBAL, nullptr, 1);
+    matvec(L.wo, m.xo, m.xb2, XS_GLOBAL, false, 1);
     norm(B, m.xb2, L.rms_ffn, A);
-    matvec(L.w13, nullptr, m.g, XS_NORMED, nullptr, 1);
-    matvec(L.w2, m.g, m.xb2, XS_GLOBAL, u, 1);
+    matvec(L.w13, nullptr, m.g, XS_NORMED, true, 1);  // m.g receives silu(gate) * up
+    matvec(L.w2, m.g, m.xb2, XS_GLOBAL, false, 1);
     delta = m.xb2;
   }
   norm(A, delta, m.rms_final, nullptr);
-  matvec(m.head, nullptr, m.logits, XS_NORMED, nullptr, 1);
+  matvec(m.head, nullptr, m.logits, XS_NORMED, false, 1);
   {
     MkPhase G{};
     G.kind = PH_ARGMAX;

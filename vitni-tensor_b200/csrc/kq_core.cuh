@@ -47,6 +47,7 @@ struct KqParams {
   KqXform xf;               // activation transform (batch 1; kind 2 needs x_smem)
   uint32_t off_ystage;      // gather: this CTA's finished rows [batch][rows_base + 1]
   uint32_t off_xsq;         // kind 2: squares of v (n floats)
+  int epi;                  // 1: rows come in (gate, up) pairs; y[b, r / 2] = silu(gate) * up
 };
 
 // quantize_block_q8 for every (batch row, superblock): one warp per block,
@@ -71,14 +72,7 @@ __device__ __forceinline__ void quantize_x(const KqParams& p, const float* xs, i
 #pragma unroll
       for (int i = 0; i < 8; i++) v[i] = src[i];
     }
-    if (p.xf.kind == 1) {  // SwiGLU: silu(g) * up
-      const float* up = p.xf.x2 + s * 256 + lane * 8;
-#pragma unroll
-      for (int i = 0; i < 8; i++) {
-        const float silu = __fdiv_rn(v[i], __fadd_rn(1.0f, libm::expf(-v[i])));
-        v[i] = __fmul_rn(silu, up[i]);
-      }
-    } else if (p.xf.kind == 2) {  // RMSNorm output (v already holds x + delta)
+    if (p.xf.kind == 2) {  // RMSNorm output (v already holds x + delta)
       const float* nw = p.xf.nw + s * 256 + lane * 8;
 #pragma unroll
       for (int i = 0; i < 8; i++) v[i] = __fmul_rn(__fmul_rn(v[i], xscale), nw[i]);
@@ -340,7 +334,17 @@ __device__ __forceinline__ void consume_pass(const KqParams& p, const uint8_t* s
 #pragma unroll
       for (int c = 0; c < NCH; c++) v[c] = part[c][b];
       const float t = seg_fixed_tree<NCH>(v, sl, p.lpr, p.S);
-      if (row_ok && sl == 0) {
+      if (p.epi) {
+        // SwiGLU of the pair, silu(g) * up with silu = g / (1 + expf(-g))
+        // (forward_quantized.rs:556-561): the up row is the next segment of
+        // this warp pass (pairs start on even rows; a pass holds an even
+        // number of rows).
+        const float up = __shfl_down_sync(0xffffffffu, t, p.lpr);
+        if (row_ok && sl == 0 && (yrow & 1) == 0) {
+          const float silu = __fdiv_rn(t, __fadd_rn(1.0f, libm::expf(-t)));
+          p.y[(int64_t)b * p.ldy + (yrow >> 1)] = __fmul_rn(silu, up);
+        }
+      } else if (row_ok && sl == 0) {
         if (p.g.world == 0)
           p.y[(int64_t)b * p.ldy + yrow] = t;
         else  // row-sharded: stage; warp 0 sends the CTA's rows at the end

@@ -71,8 +71,9 @@ __global__ void __launch_bounds__((CW + 1) * 32, VTQ_KQ_CTAS) kq_matvec_kernel(c
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int bid = blockIdx.x;
-  const int r0 = bid * p.rows_base + min(bid, p.rows_rem);
-  const int nrows = p.rows_base + (bid < p.rows_rem ? 1 : 0);
+  const int unit = p.epi ? 2 : 1;  // rows are dealt to CTAs in (gate, up) pairs for the epilogue
+  const int r0 = unit * (bid * p.rows_base + min(bid, p.rows_rem));
+  const int nrows = unit * (p.rows_base + (bid < p.rows_rem ? 1 : 0));
   const int nstages = (nrows + p.rps - 1) / p.rps;
 
   if (tid == 0) {
@@ -358,6 +359,7 @@ cudaError_t launch_kq_matvec(const DevMatrix& m, const float* x, int64_t ldx, in
   const int rpw = 32 / lpr;
   const int grid = (int)std::min<int64_t>(m.out_feat, nsm);
   for (int64_t b0 = 0; b0 < batch; b0 += KQ_BMAX) {
+    int grid_l = grid;
     const int nb = (int)std::min<int64_t>(KQ_BMAX, batch - b0);
     KqParams p{};
     p.x = x + b0 * ldx;
@@ -378,9 +380,18 @@ cudaError_t launch_kq_matvec(const DevMatrix& m, const float* x, int64_t ldx, in
       p.g = *g;
     }
     if (xform && xform->kind) {
-      if (batch != 1 || (xform->kind == 1 && !xform->x2) || (xform->kind == 2 && !xform->nw))
-        return cudaErrorInvalidValue;
+      if (batch != 1 || xform->kind != 2 || !xform->nw) return cudaErrorInvalidValue;
       p.xf = *xform;
+    }
+    if (xform && xform->swiglu_pairs) {
+      // Rows interleaved (gate_i, up_i): pairs dealt to CTAs, both rows of a
+      // pair in one warp pass.
+      if (g || p.R % 2 || rpw < 2) return cudaErrorInvalidValue;
+      p.epi = 1;
+      const int gp = std::min(p.R / 2, nsm);
+      p.rows_base = (p.R / 2) / gp;
+      p.rows_rem = (p.R / 2) % gp;
+      grid_l = gp;
     }
     p.lpr = lpr;
     const int NB = m.dtype == T_Q4_K ? BsumStride<8>::v : BsumStride<16>::v;
@@ -410,7 +421,7 @@ cudaError_t launch_kq_matvec(const DevMatrix& m, const float* x, int64_t ldx, in
     }
     p.off_stage = off;
     // Stages of ~24 KB of whole warp passes (TMA streams at full rate from 16 KB).
-    const int rows_per_cta = p.rows_base + (p.rows_rem ? 1 : 0);
+    const int rows_per_cta = (p.epi ? 2 : 1) * (p.rows_base + (p.rows_rem ? 1 : 0));
     int rps = std::max(rpw, (int)(24576 / m.pitch) / rpw * rpw);
     rps = std::min(rps, (rows_per_cta + rpw - 1) / rpw * rpw);
     int nst;
@@ -430,8 +441,8 @@ cudaError_t launch_kq_matvec(const DevMatrix& m, const float* x, int64_t ldx, in
     p.rps = rps;
     p.nst = nst;
     const uint32_t smem = p.off_stage + (uint32_t)nst * p.stage_bytes;
-    const cudaError_t e = m.dtype == T_Q4_K ? launch_qt<0>(p, grid, smem, st)
-                                            : launch_qt<1>(p, grid, smem, st);
+    const cudaError_t e = m.dtype == T_Q4_K ? launch_qt<0>(p, grid_l, smem, st)
+                                            : launch_qt<1>(p, grid_l, smem, st);
     if (e != cudaSuccess) return e;
   }
   return cudaSuccess;

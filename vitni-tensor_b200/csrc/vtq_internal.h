@@ -58,9 +58,13 @@ struct GatherTarget {
 //   kind 2 RMSNorm v_i = x_i (+ delta_i); x_i = (v_i * scale) * nw_i with
 //                  scale = 1 / sqrtf(sum(v^2) / n + eps), the sum serial
 //                  (rms_norm.rs:94-108); CTA 0 stores v to res_out if set.
+// Activation transform of a k-quant matvec (batch 1): kind 2 = RMSNorm of
+// v = x + delta (written to res_out) scaled by nw, computed in the prologue.
+// swiglu_pairs: the matrix rows are (gate_i, up_i) pairs and y receives
+// silu(gate_i) * up_i (R / 2 values) from the epilogue.
 struct KqXform {
   int kind = 0;
-  const float* x2 = nullptr;
+  int swiglu_pairs = 0;
   const float* delta = nullptr;
   const float* nw = nullptr;
   float eps = 0.0f;
