@@ -38,13 +38,20 @@ namespace {
 // selected by their output pointer (set by a host-side probe).
 __device__ unsigned long long g_kq_trace[8][1024][8];
 __device__ const float* g_kq_trace_y[8];
+__device__ unsigned long long g_kq_arrive[8][1024][16];  // stage k full (k < 15), 15: x ready
 #define KQ_TRACE(slot)                                                      \
   do {                                                                      \
     for (int ti_ = 0; ti_ < 8; ti_++)                                       \
       if (g_kq_trace_y[ti_] == p.y) g_kq_trace[ti_][blockIdx.x][slot] = globaltimer(); \
   } while (0)
+#define KQ_ARRIVE(k)                                                        \
+  do {                                                                      \
+    for (int ti_ = 0; ti_ < 8; ti_++)                                       \
+      if (g_kq_trace_y[ti_] == p.y && (k) < 16) g_kq_arrive[ti_][blockIdx.x][k] = globaltimer(); \
+  } while (0)
 #else
 #define KQ_TRACE(slot) (void)0
+#define KQ_ARRIVE(k) (void)0
 #endif
 
 #ifndef VTQ_KQ_CTAS
@@ -56,6 +63,7 @@ __device__ const float* g_kq_trace_y[8];
 #ifndef VTQ_KQ_CW1
 #define VTQ_KQ_CW1 16
 #endif
+
 template <int QT, int MAXB, int NCH, int CW>
 __global__ void __launch_bounds__((CW + 1) * 32, VTQ_KQ_CTAS) kq_matvec_kernel(const KqParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
@@ -78,7 +86,6 @@ __global__ void __launch_bounds__((CW + 1) * 32, VTQ_KQ_CTAS) kq_matvec_kernel(c
 
   if (tid == 0) {
     KQ_TRACE(0);
-    KQ_TRACE(6);
     for (int i = 0; i < p.nst; i++) {
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], CW);
@@ -104,7 +111,9 @@ __global__ void __launch_bounds__((CW + 1) * 32, VTQ_KQ_CTAS) kq_matvec_kernel(c
       // stages before waiting on the previous grid (programmatic launch).
       const int first = min(p.nst, nstages);
       if (first > 0) issue(0);
+      KQ_TRACE(6);
       grid_dep_wait();
+      KQ_TRACE(7);
       if (p.x_smem) {
         const uint32_t rowb = (uint32_t)p.n * 4u;
         mbar_arrive_expect_tx(xbar, rowb * p.batch);
@@ -194,6 +203,7 @@ __global__ void __launch_bounds__((CW + 1) * 32, VTQ_KQ_CTAS) kq_matvec_kernel(c
       if (lane == 0) record_error(p.status, KERR_TIMEOUT);
       return;
     }
+    if (tid == 0 && k < 15) KQ_ARRIVE(k);
     if (g < gend) {
       if (tid == 0 && k == 0) KQ_TRACE(3);
       const uint8_t* sbuf = stg + (size_t)buf * p.stage_bytes;

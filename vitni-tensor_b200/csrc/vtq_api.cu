@@ -5,6 +5,7 @@
 // point replaces (vitni-tensor src/ops/quant.rs, src/model/forward_quantized.rs)
 // so a caller sees the same failure for the same bad input. There is no CPU
 // fallback: every arithmetic result comes from the sm_100a kernels.
+#include <chrono>
 #include <cstdio>
 #include <cstring>
 #include <string>
@@ -21,6 +22,10 @@ struct vtq_ctx {
   // io buffer: [status word | 252 B pad][y capacity][x capacity]
   uint8_t* io = nullptr;
   size_t io_cap = 0;
+  // pinned host staging for host-pointer calls whose buffers are not pinned
+  uint8_t* hio = nullptr;
+  size_t hio_cap = 0;
+  cudaEvent_t done = nullptr;  // end of a host-pointer call (polled, not blocked on)
   std::string err;
 };
 
@@ -105,6 +110,50 @@ vtq_status check_kernel_limits(vtq_ctx* c, const DevMatrix& m, uint32_t flags) {
 }
 
 // Host-pointer linear on a device-resident matrix: x in, kernel, y+status out.
+// Page-locked (cudaHostAlloc'd or registered) host memory: copies to and from
+// it run as asynchronous DMA; pageable memory goes through the context's
+// pinned staging buffer instead.
+bool host_pinned(const void* p) {
+  cudaPointerAttributes a{};
+  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  return a.type == cudaMemoryTypeHost;
+}
+
+vtq_status ensure_hio(vtq_ctx* c, size_t need) {
+  if (need <= c->hio_cap) return VTQ_OK;
+  const size_t cap = (std::max(need, c->hio_cap * 2) + 4095) / 4096 * 4096;
+  if (c->hio) {
+    VTQ_CUDA(c, cudaStreamSynchronize(c->stream));
+    cudaFreeHost(c->hio);
+    c->hio = nullptr;
+    c->hio_cap = 0;
+  }
+  VTQ_CUDA(c, cudaHostAlloc(&c->hio, cap, cudaHostAllocDefault));
+  c->hio_cap = cap;
+  return VTQ_OK;
+}
+
+// Wait for everything enqueued on the context stream by polling an event: a
+// host-pointer call is short and latency-bound, so the calling thread spins
+// instead of sleeping in the driver.
+vtq_status wait_call(vtq_ctx* c) {
+  if (!c->done) VTQ_CUDA(c, cudaEventCreateWithFlags(&c->done, cudaEventDisableTiming));
+  VTQ_CUDA(c, cudaEventRecord(c->done, c->stream));
+  const auto t0 = std::chrono::steady_clock::now();
+  for (unsigned i = 0;; i++) {
+    const cudaError_t e = cudaEventQuery(c->done);
+    if (e == cudaSuccess) return VTQ_OK;
+    if (e != cudaErrorNotReady) VTQ_CUDA(c, e);
+    // Device-side waits are bounded at 2 s; a call still running after a
+    // minute means the device stopped answering.
+    if ((i & 1023) == 1023 && std::chrono::steady_clock::now() - t0 > std::chrono::seconds(60))
+      return fail(c, VTQ_ERR_TIMEOUT, "vtq_linear: the device did not finish the call in 60 s");
+  }
+}
+
 vtq_status linear_host(vtq_ctx* c, const DevMatrix& m, const float* x, float* y, int64_t batch,
                        uint32_t flags) {
   if (vtq_status s = check_kernel_limits(c, m, flags)) return s;
@@ -114,23 +163,29 @@ vtq_status linear_host(vtq_ctx* c, const DevMatrix& m, const float* x, float* y,
   float* dx = reinterpret_cast<float*>(c->io + xoff);
   float* dy = reinterpret_cast<float*>(c->io + yoff);
   unsigned* dstat = reinterpret_cast<unsigned*>(c->io);
-  VTQ_CUDA(c, cudaMemcpyAsync(dx, x, xbytes, cudaMemcpyHostToDevice, c->stream));
-  VTQ_CUDA(c, run_linear(m, dx, m.in_feat, dy, m.out_feat, batch, flags, dstat, c->stream));
-  // One D2H copy brings back the status word and y together.
-  std::string tmp;
-  const size_t back = yoff + ybytes;
-  uint32_t statbuf[kStatusBytes / 4];
-  if (back <= 64 * 1024) {
-    uint8_t host[64 * 1024];
-    VTQ_CUDA(c, cudaMemcpyAsync(host, c->io, back, cudaMemcpyDeviceToHost, c->stream));
-    VTQ_CUDA(c, cudaStreamSynchronize(c->stream));
-    memcpy(statbuf, host, kStatusBytes);
-    memcpy(y, host + yoff, ybytes);
+  const bool x_pinned = host_pinned(x), y_pinned = host_pinned(y);
+  // Staging layout: [status | y][x], the device io buffer's layout.
+  if (vtq_status s = ensure_hio(c, (y_pinned ? kStatusBytes : yoff + ybytes) +
+                                       (x_pinned ? 0 : xoff + xbytes)))
+    return s;
+  if (x_pinned) {
+    VTQ_CUDA(c, cudaMemcpyAsync(dx, x, xbytes, cudaMemcpyHostToDevice, c->stream));
   } else {
-    VTQ_CUDA(c, cudaMemcpyAsync(statbuf, c->io, kStatusBytes, cudaMemcpyDeviceToHost, c->stream));
-    VTQ_CUDA(c, cudaMemcpyAsync(y, dy, ybytes, cudaMemcpyDeviceToHost, c->stream));
-    VTQ_CUDA(c, cudaStreamSynchronize(c->stream));
+    memcpy(c->hio + xoff, x, xbytes);
+    VTQ_CUDA(c, cudaMemcpyAsync(dx, c->hio + xoff, xbytes, cudaMemcpyHostToDevice, c->stream));
   }
+  VTQ_CUDA(c, run_linear(m, dx, m.in_feat, dy, m.out_feat, batch, flags, dstat, c->stream));
+  uint32_t statbuf[kStatusBytes / 4];
+  if (y_pinned) {
+    VTQ_CUDA(c, cudaMemcpyAsync(c->hio, c->io, kStatusBytes, cudaMemcpyDeviceToHost, c->stream));
+    VTQ_CUDA(c, cudaMemcpyAsync(y, dy, ybytes, cudaMemcpyDeviceToHost, c->stream));
+  } else {
+    // One D2H copy brings back the status word and y together.
+    VTQ_CUDA(c, cudaMemcpyAsync(c->hio, c->io, yoff + ybytes, cudaMemcpyDeviceToHost, c->stream));
+  }
+  if (vtq_status s = wait_call(c)) return s;
+  if (!y_pinned) memcpy(y, c->hio + yoff, ybytes);
+  memcpy(statbuf, c->hio, kStatusBytes);
   if (statbuf[0] != 0) {
     VTQ_CUDA(c, cudaMemsetAsync(c->io, 0, 4, c->stream));
     return fail(c, VTQ_ERR_TIMEOUT, "vtq_linear: a device-side wait timed out");
@@ -233,6 +288,8 @@ vtq_status vtq_destroy(vtq_ctx* c) {
   cudaSetDevice(c->device);
   cudaStreamSynchronize(c->stream);
   if (c->io) cudaFree(c->io);
+  if (c->hio) cudaFreeHost(c->hio);
+  if (c->done) cudaEventDestroy(c->done);
   if (c->own) cudaStreamDestroy(c->own);
   delete c;
   return VTQ_OK;
