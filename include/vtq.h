@@ -143,7 +143,7 @@ vtq_status vtq_linear_host_noalloc(int32_t dtype, const uint8_t* w_dev, int64_t 
                                    int64_t rows, const float* x, float* y, int64_t batch,
                                    void* cuda_stream);
 
-/* ---- Quantized decode session: a GGUF Llama model resident on
+/* ---- Quantized decode session: a GGUF Llama or Qwen2 model resident on
  * one device; the decode step of src/model/forward_quantized.rs:329-649 and the
  * prompt + greedy loop of src/model/inference.rs:312-327 run as one CUDA graph
  * per step with the position and current token in device memory. ---- */

@@ -208,13 +208,16 @@ class _Tensor(ctypes.Structure):
 
 class _Layer(ctypes.Structure):
     _fields_ = [("rms_att", ctypes.c_void_p), ("rms_ffn", ctypes.c_void_p)] + \
-        [(n, _Tensor) for n in ("wq", "wk", "wv", "wo", "w1", "w2", "w3")]
+        [(n, _Tensor) for n in ("wq", "wk", "wv", "wo", "w1", "w2", "w3")] + \
+        [(n, ctypes.c_void_p) for n in ("bq", "bk", "bv")] + \
+        [(n, ctypes.c_int32) for n in ("bq_len", "bk_len", "bv_len")]
 
 
 class _Model(ctypes.Structure):
     _fields_ = [(n, ctypes.c_int32) for n in ("dim", "hidden", "n_layers", "n_heads",
                                                "n_kv_heads", "vocab", "seq_len")] + \
-        [("rope_theta", ctypes.c_float), ("rms_eps", ctypes.c_float), ("embd", _Tensor),
+        [("rope_theta", ctypes.c_float), ("rms_eps", ctypes.c_float),
+         ("rope_neox", ctypes.c_int32), ("embd", _Tensor),
          ("rms_final", ctypes.c_void_p), ("wcls", _Tensor), ("layers", ctypes.c_void_p)]
 
 
@@ -249,6 +252,7 @@ def decode_run(gguf_blob: bytes, prompt, n_new: int, threads: int = 8, logits: b
     m.seq_len = meta[f"{arch}.context_length"]
     m.rope_theta = meta.get(f"{arch}.rope.freq_base", 10000.0)
     m.rms_eps = meta.get(f"{arch}.attention.layer_norm_rms_epsilon", 1e-5)
+    m.rope_neox = 1 if arch == "qwen2" else 0  # quant_weights.rs:151
     m.embd = tensor("token_embd.weight")
     m.rms_final = addr("output_norm.weight")[0]
     m.wcls = tensor("output.weight") if "output.weight" in ts else _Tensor(0, None, 0)
@@ -261,6 +265,11 @@ def decode_run(gguf_blob: bytes, prompt, n_new: int, threads: int = 8, logits: b
                         ("wo", "attn_output"), ("w1", "ffn_gate"), ("w2", "ffn_down"),
                         ("w3", "ffn_up")):
             setattr(layers[l], fld, tensor(p + nm + ".weight"))
+        for fld, nm in (("bq", "attn_q"), ("bk", "attn_k"), ("bv", "attn_v")):
+            if p + nm + ".bias" in ts:  # optional QKV bias (quant_weights.rs:172-174)
+                a, n = addr(p + nm + ".bias")
+                setattr(layers[l], fld, a)
+                setattr(layers[l], fld + "_len", n // 4)
     m.layers = ctypes.cast(layers, ctypes.c_void_p)
     pr = np.ascontiguousarray(prompt, dtype=np.uint32)
     out = np.zeros(max(1, n_new), np.uint32)

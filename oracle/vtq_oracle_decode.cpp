@@ -2,8 +2,9 @@
 // step and prompt+generate loop.
 //
 // TEST INFRASTRUCTURE ONLY: the checker for the device decode session.
-//   step            src/model/forward_quantized.rs:329-649 (Llama path: interleaved
-//                   RoPE, no QKV bias, separate or shared LM head)
+//   step            src/model/forward_quantized.rs:329-649 (interleaved RoPE for
+//                   Llama, NeoX split-half RoPE for Qwen2 (:414-448), optional
+//                   QKV bias (add_bias :807-813), separate or shared LM head)
 //   embedding_row   src/model/forward_quantized.rs:818-919
 //   softmax_inplace src/model/forward_quantized.rs:925-941
 //   rms_norm_slice  src/ops/rms_norm.rs:94-108
@@ -32,11 +33,14 @@ typedef struct {
   const float* rms_att;
   const float* rms_ffn;
   or_tensor wq, wk, wv, wo, w1, w2, w3;
+  const float *bq, *bk, *bv;  // NULL when absent; else bq_len / bk_len / bv_len entries
+  int32_t bq_len, bk_len, bv_len;
 } or_layer;
 
 typedef struct {
   int32_t dim, hidden, n_layers, n_heads, n_kv_heads, vocab, seq_len;
   float rope_theta, rms_eps;
+  int32_t rope_neox;  // quant_weights.rs:151: architecture "qwen2"
   or_tensor embd;
   const float* rms_final;
   or_tensor wcls;  // bytes == NULL: the head shares token_embd
@@ -97,6 +101,12 @@ void softmax_inplace(float* x, int n) {
   for (int i = 0; i < n; i++) x[i] *= inv;
 }
 
+// add_bias (forward_quantized.rs:807-813): v[i] += b[i] over the shorter length.
+void add_bias(float* v, int n, const float* b, int blen) {
+  if (!b) return;
+  for (int i = 0; i < n && i < blen; i++) v[i] = v[i] + b[i];
+}
+
 int step(State& st, uint32_t token, int pos, float* logits) {
   const or_model& m = *st.m;
   const int dim = m.dim, hs = dim / m.n_heads, kv_dim = m.n_kv_heads * hs;
@@ -111,13 +121,35 @@ int step(State& st, uint32_t token, int pos, float* logits) {
     if ((s = linear(xb.data(), L.wq, dim, dim, q.data(), st.threads))) return s;
     if ((s = linear(xb.data(), L.wk, dim, kv_dim, k.data(), st.threads))) return s;
     if ((s = linear(xb.data(), L.wv, dim, kv_dim, v.data(), st.threads))) return s;
+    add_bias(q.data(), dim, L.bq, L.bq_len);
+    add_bias(k.data(), kv_dim, L.bk, L.bk_len);
+    add_bias(v.data(), kv_dim, L.bv, L.bv_len);
     const size_t off = ((size_t)l * m.seq_len + pos) * kv_dim;
     float* kc = st.key_cache.data();
     float* vc = st.value_cache.data();
     memcpy(kc + off, k.data(), kv_dim * 4);
     memcpy(vc + off, v.data(), kv_dim * 4);
+    if (m.rope_neox) {
+      // NeoX RoPE: pairs (j, j + hs/2) within each head, q heads then cached k heads.
+      const int half = hs / 2;
+      for (int pass = 0; pass < 2; pass++) {
+        const int nh = pass == 0 ? m.n_heads : kv_dim / hs;
+        float* base0 = pass == 0 ? q.data() : kc + off;
+        for (int h = 0; h < nh; h++) {
+          float* b = base0 + h * hs;
+          for (int j = 0; j < half; j++) {
+            const float freq = 1.0f / vtq::libm::powf(m.rope_theta, (float)(2 * j) / (float)hs);
+            const float val = (float)pos * freq;
+            const float fcr = vtq::libm::cosf(val), fci = vtq::libm::sinf(val);
+            const float a = b[j], c = b[j + half];
+            b[j] = a * fcr - c * fci;
+            b[j + half] = a * fci + c * fcr;
+          }
+        }
+      }
+    }
     // Interleaved RoPE on q (all of dim) and on the cached k (i < kv_dim).
-    for (int i = 0; i < dim; i += 2) {
+    for (int i = 0; i < dim && !m.rope_neox; i += 2) {
       const int idx = i % hs;
       const float freq = 1.0f / vtq::libm::powf(m.rope_theta, (float)idx / (float)hs);
       const float val = (float)pos * freq;

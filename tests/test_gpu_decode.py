@@ -44,19 +44,33 @@ def assert_bits(a, b):
     assert bad.size == 0, f"{bad.size} logits differ; first {bad[:4]}"
 
 
-@pytest.mark.parametrize("variant", ["q4k_embd", "q6k_embd", "shared_head", "mha"])
+@pytest.mark.parametrize("variant", ["q4k_embd", "q6k_embd", "shared_head", "mha", "qwen2",
+                                     "qwen2_q5"])
 def test_small_models_bit_exact(variant, step_path):
     cfg = dict(SMALL)
     kw = {}
+    kind = step_path
     if variant == "q6k_embd":
         kw["embd_dtype"] = vtq.Q6_K
     if variant == "shared_head":
         kw["shared_head"] = True
     if variant == "mha":
         cfg.update(kv_heads=4, hidden=768, layers=3)
+    if variant.startswith("qwen2"):
+        # Qwen2: NeoX RoPE, QKV bias, rope base 1e6, eps 1e-6 (quant_weights.rs:143-151)
+        cfg.update(rope_theta=1e6, rms_eps=1e-6)
+        kw.update(arch="qwen2", qkv_bias=True)
+    if variant == "qwen2_q5":
+        # Qwen2.5-style formats: the linears run on the canonical fp32 kernels,
+        # so every step path falls back to the per-op graph (kind 0)
+        kw["wdtypes"] = {"attn_q": vtq.Q5_0, "attn_k": vtq.Q5_0, "attn_v": vtq.Q8_0,
+                         "attn_output": vtq.Q5_0, "ffn_gate": vtq.Q5_0, "ffn_up": vtq.Q5_0,
+                         "ffn_down": vtq.Q8_0}
+        kw["embd_dtype"] = vtq.Q8_0
+        kind = 0
     blob = gguf.synthetic_llama(cfg, seed=3, **kw)
     prompt = gguf.prompt_tokens(7, cfg["vocab"], seed=1)
-    got, lg, again, ref, rlg = run_both(blob, prompt, 9, step_path)
+    got, lg, again, ref, rlg = run_both(blob, prompt, 9, kind)
     assert_bits(lg, rlg)
     assert got == ref and again == ref
 

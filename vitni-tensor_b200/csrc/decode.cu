@@ -16,6 +16,7 @@
 //   SwiGLU/softmax expf restated on the device (vtq_libm.h)
 #include <cuda_fp16.h>
 
+#include <algorithm>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -292,13 +293,13 @@ __global__ void __launch_bounds__(256) rmsnorm_res_kernel(const float* x, const 
 __global__ void attention_rope_kernel(const float* q, const float* k, const float* v, float* kc,
                                       float* vc, int layer, int seq_len, int kv_dim, int hs,
                                       int kv_mul, const float* rcos, const float* rsin,
-                                      const StepState* st, float* out) {
+                                      const StepState* st, float* out, AttnExtras ex) {
   extern __shared__ float sm[];
   __shared__ float red[2];
   pdl_wait();
   pdl_release();
   attention_head(blockIdx.x, q, k, v, kc, vc, layer, seq_len, kv_dim, hs, kv_mul, rcos, rsin,
-                 st->pos, out, sm, red, threadIdx.x, blockDim.x, [] { __syncthreads(); });
+                 st->pos, out, sm, red, threadIdx.x, blockDim.x, [] { __syncthreads(); }, ex);
 }
 
 // SwiGLU: silu(g) * up with silu = g / (1 + expf(-g)) (forward_quantized.rs:556-561).
@@ -345,10 +346,12 @@ struct vtq_decode {
   int dim = 0, hidden = 0, n_layers = 0, n_heads = 0, n_kv_heads = 0, vocab = 0, seq_len = 0;
   bool shared = false;
   float rope_theta = 10000.0f, rms_eps = 1e-5f;
+  bool neox = false;  // NeoX split-half RoPE (architecture "qwen2", quant_weights.rs:151)
   std::vector<void*> allocs;
   DevMatrix embd{}, head{};
   struct Layer {
     float *rms_att, *rms_ffn;
+    float *bq = nullptr, *bk = nullptr, *bv = nullptr;  // Qwen2 QKV biases (-0.0 padded)
     DevMatrix wq, wk, wv, wo, w1, w2, w3;
     // q|k and gate|up share their input: when each pair has one dtype, the two
     // matrices sit back to back in HBM and run as one launch (wqk, w13).
@@ -514,7 +517,7 @@ vtq_status enqueue_step(vtq_decode* d, bool log_logits) {
       }
       DCUDA(d, launch_pdl(attention_rope_kernel, d->n_heads, 128, att_smem, s, d->q, d->k, d->v,
                           d->kc, d->vc, l, d->seq_len, kv_dim, hs, kv_mul, d->rcos, d->rsin,
-                          d->st, d->xo));
+                          d->st, d->xo, AttnExtras{d->neox ? 1 : 0, L.bq, L.bk, L.bv}));
       DCUDA(d, mv(L.wo, d->xo, d->xb2, s, nullptr));
       if (fz & 2) {
         KqXform ffn;
@@ -568,7 +571,7 @@ vtq_status enqueue_step(vtq_decode* d, bool log_logits) {
     DCUDA(d, cudaStreamWaitEvent(s, d->join, 0));
     DCUDA(d, launch_pdl(attention_rope_kernel, d->n_heads, 128, att_smem, s, d->q, d->k, d->v,
                         d->kc, d->vc, l, d->seq_len, kv_dim, hs, kv_mul, d->rcos, d->rsin, d->st,
-                        d->xo));
+                        d->xo, AttnExtras{d->neox ? 1 : 0, L.bq, L.bk, L.bv}));
     DCUDA(d, launch_kq_or_canon(L.wo, d->xo, d->xb2, d->status, s));
     DCUDA(d, launch_pdl(rmsnorm_kernel, 1, 256, rms_smem, s, d->x, d->xb2, L.rms_ffn,
                         d->rms_eps, dim, d->xb));
@@ -630,8 +633,8 @@ vtq_status vtq_decode_open(vtq_ctx* ctx, int device, const uint8_t* gguf, size_t
   if (arch_it == g.meta.end() || arch_it->second.type != 8)
     return dfail(d, VTQ_ERR_INTERNAL, "gguf: missing 'general.architecture' metadata");
   const std::string arch = arch_it->second.s;
-  if (arch != "llama")
-    return dfail(d, VTQ_ERR_NOT_IMPLEMENTED, "decode session: only the llama architecture");
+  // Any architecture string keys the metadata (config.rs:141-165); "qwen2"
+  // selects NeoX RoPE below, every other one the Llama layout.
   bool ok = true;
   d->dim = (int)meta_uint(g, arch + ".embedding_length", &ok);
   d->hidden = (int)meta_uint(g, arch + ".feed_forward_length", &ok);
@@ -653,6 +656,7 @@ vtq_status vtq_decode_open(vtq_ctx* ctx, int device, const uint8_t* gguf, size_t
   };
   d->rope_theta = f32meta(arch + ".rope.freq_base", 10000.0f);
   d->rms_eps = f32meta(arch + ".attention.layer_norm_rms_epsilon", 1e-5f);
+  d->neox = arch == "qwen2";
   if (d->dim <= 0 || d->n_heads <= 0 || d->dim % d->n_heads || d->n_kv_heads <= 0 ||
       d->n_heads % d->n_kv_heads || (d->dim / d->n_heads) % 2 || d->dim > 8192 ||
       d->seq_len <= 0 || d->vocab <= 0)
@@ -674,8 +678,27 @@ vtq_status vtq_decode_open(vtq_ctx* ctx, int device, const uint8_t* gguf, size_t
     const std::string p = "blk." + std::to_string(l) + ".";
     if ((s = upload_f32(d, g, p + "attn_norm.weight", dim, &L.rms_att))) return s;
     if ((s = upload_f32(d, g, p + "ffn_norm.weight", dim, &L.rms_ffn))) return s;
-    if (g.tensors.count(p + "attn_q.bias"))
-      return dfail(d, VTQ_ERR_NOT_IMPLEMENTED, "decode session: QKV bias (Qwen2) not supported");
+    // Optional QKV biases (quant_weights.rs:172-174, F32). add_bias zips with the
+    // shorter length (forward_quantized.rs:807-813): entries past the tensor are
+    // padded with -0.0, which adds nothing to any value.
+    struct {
+      const char* name;
+      int n;
+      float** dst;
+    } biases[] = {{"attn_q.bias", dim, &L.bq}, {"attn_k.bias", kv_dim, &L.bk},
+                  {"attn_v.bias", kv_dim, &L.bv}};
+    for (auto& b : biases) {
+      auto it = g.tensors.find(p + b.name);
+      if (it == g.tensors.end()) continue;
+      if (it->second.dtype != T_F32)
+        return dfail(d, VTQ_ERR_INTERNAL, "gguf: expected F32 bias tensor");
+      if (it->second.len % 4)
+        return dfail(d, VTQ_ERR_INTERNAL, "gguf: F32 bias byte length not a multiple of 4");
+      std::vector<float> h(b.n, -0.0f);
+      memcpy(h.data(), it->second.bytes, std::min<size_t>(it->second.len, (size_t)b.n * 4));
+      if (vtq_status e = dalloc(d, b.dst, (size_t)b.n * 4)) return e;
+      DCUDA(d, cudaMemcpy(*b.dst, h.data(), (size_t)b.n * 4, cudaMemcpyHostToDevice));
+    }
     struct {
       const char* name;
       int64_t in, out;
@@ -793,7 +816,9 @@ vtq_status vtq_decode_open(vtq_ctx* ctx, int device, const uint8_t* gguf, size_t
     mm.embd = d->embd;
     mm.head = d->head;
     mm.rms_final = d->rms_final;
-    for (auto& L : d->layers) mm.layers.push_back({L.wqk, L.wv, L.wo, L.w13, L.w2, L.rms_att, L.rms_ffn});
+    for (auto& L : d->layers)
+      mm.layers.push_back({L.wqk, L.wv, L.wo, L.w13, L.w2, L.rms_att, L.rms_ffn, L.bq, L.bk, L.bv});
+    mm.neox = d->neox;
     mm.x = d->x;
     mm.xr = d->xr;
     mm.q = d->q;

@@ -65,6 +65,7 @@ struct MkPhase {
   int xsrc;  // XS_GLOBAL: kp.x, XS_NORMED: the NORM result
   // ATTN
   int layer;
+  const float *bq, *bk, *bv;
 };
 
 struct MkArgs {
@@ -74,7 +75,7 @@ struct MkArgs {
   unsigned* status;
   StepState* st;
   // model
-  int dim, hs, kv_dim, kv_mul, n_heads, seq_len, vocab;
+  int dim, hs, kv_dim, kv_mul, n_heads, seq_len, vocab, neox;
   float eps;
   const uint8_t* embd;
   int embd_dtype;
@@ -243,7 +244,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_mk_kernel(const MkArgs a
       if (bid < a.n_heads)
         attention_head(bid, a.q, a.k, a.v, a.kc, a.vc, ph.layer, a.seq_len, a.kv_dim, a.hs,
                        a.kv_mul, a.rcos, a.rsin, a.st->pos, a.xo, xsq, red, tid, MK_CW * 32,
-                       [] { cons_sync(); });
+                       [] { cons_sync(); }, AttnExtras{a.neox, ph.bq, ph.bk, ph.bv});
     } else if (ph.kind == PH_ARGMAX) {
       if (a.log)  // every CTA copies a slice of the step's logits to the log
         for (int i = bid * MK_CW * 32 + tid; i < a.vocab; i += gridDim.x * MK_CW * 32)
@@ -440,6 +441,9 @@ cudaError_t mk_build(const MkModel& m, MkPlan** out) {
     At.kind = PH_ATTN;
     At.barrier = 1;
     At.layer = l;
+    At.bq = L.bq;
+    At.bk = L.bk;
+    At.bv = L.bv;
     ph.push_back(At);
     matvec(L.wo, m.xo, m.xb2, XS_GLOBAL, false, 1);
     norm(B, m.xb2, L.rms_ffn, A);
@@ -490,6 +494,7 @@ cudaError_t mk_build(const MkModel& m, MkPlan** out) {
   a.seq_len = m.seq_len;
   a.vocab = m.vocab;
   a.eps = m.eps;
+  a.neox = m.neox ? 1 : 0;
   a.embd = m.embd.data;
   a.embd_dtype = m.embd.dtype;
   a.embd_pitch = m.embd.pitch;

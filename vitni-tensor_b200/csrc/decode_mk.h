@@ -22,11 +22,13 @@ struct StepState {  // device-resident per-run state
 struct MkLayer {
   DevMatrix wqk, wv, wo, w13, w2;
   const float *rms_att, *rms_ffn;
+  const float *bq, *bk, *bv;  // QKV biases or null
 };
 
 struct MkModel {
   int dim, hidden, n_layers, n_heads, n_kv_heads, vocab, seq_len;
   float eps;
+  bool neox;  // NeoX RoPE (Qwen2)
   DevMatrix embd, head;
   const float* rms_final;
   std::vector<MkLayer> layers;

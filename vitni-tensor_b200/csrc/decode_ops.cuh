@@ -12,6 +12,13 @@
 namespace vtq {
 namespace {
 
+// Qwen2 additions to the attention step: NeoX RoPE and the QKV biases
+// (device vectors of the q / kv widths, or null).
+struct AttnExtras {
+  int neox;
+  const float *bq, *bk, *bv;
+};
+
 // embedding_row (forward_quantized.rs:818-919): element e of row `row` of the
 // table in its device layout (Q6_K regrouped, see repack.cu).
 __device__ __forceinline__ float embed_value(const uint8_t* table, int dtype, int64_t pitch,
@@ -72,30 +79,50 @@ __device__ __forceinline__ void attention_head(int h, const float* q, const floa
                                                int seq_len, int kv_dim, int hs, int kv_mul,
                                                const float* rcos, const float* rsin, int pos,
                                                float* out, float* sm, float* red, int tid,
-                                               int nthr, Sync sync) {
+                                               int nthr, Sync sync, const AttnExtras& ex) {
   float* qh = sm;            // [hs] rotated query head
   float* kh = sm + hs;       // [hs] rotated new key
   float* vh = sm + 2 * hs;   // [hs] new value
   float* att = sm + 3 * hs;  // [pos + 1]
   const int g = h / kv_mul, np = pos + 1;
   const size_t off = ((size_t)layer * seq_len + pos) * kv_dim;
-  for (int p = tid; p < hs / 2; p += nthr) {
-    const float fcr = rcos[(size_t)pos * (hs / 2) + p], fci = rsin[(size_t)pos * (hs / 2) + p];
-    const float q0 = q[h * hs + 2 * p], q1 = q[h * hs + 2 * p + 1];
-    qh[2 * p] = __fsub_rn(__fmul_rn(q0, fcr), __fmul_rn(q1, fci));
-    qh[2 * p + 1] = __fadd_rn(__fmul_rn(q0, fci), __fmul_rn(q1, fcr));
-    const float k0 = k[g * hs + 2 * p], k1 = k[g * hs + 2 * p + 1];
+  // Pair p of the head: elements (2p, 2p + 1) for Llama's interleaved RoPE,
+  // (p, p + hs/2) for NeoX (Qwen2, forward_quantized.rs:417-448). Both use
+  // freq = 1 / powf(theta, 2p / hs), so one cos/sin table serves both. The
+  // optional QKV bias is added first (add_bias, :807-813; pad entries are
+  // -0.0, which leaves every value unchanged).
+  const int half = hs / 2;
+  for (int p = tid; p < half; p += nthr) {
+    const int e0 = ex.neox ? p : 2 * p, e1 = ex.neox ? p + half : 2 * p + 1;
+    const float fcr = rcos[(size_t)pos * half + p], fci = rsin[(size_t)pos * half + p];
+    float q0 = q[h * hs + e0], q1 = q[h * hs + e1];
+    float k0 = k[g * hs + e0], k1 = k[g * hs + e1];
+    float v0 = v[g * hs + e0], v1 = v[g * hs + e1];
+    if (ex.bq) {
+      q0 = __fadd_rn(q0, ex.bq[h * hs + e0]);
+      q1 = __fadd_rn(q1, ex.bq[h * hs + e1]);
+    }
+    if (ex.bk) {
+      k0 = __fadd_rn(k0, ex.bk[g * hs + e0]);
+      k1 = __fadd_rn(k1, ex.bk[g * hs + e1]);
+    }
+    if (ex.bv) {
+      v0 = __fadd_rn(v0, ex.bv[g * hs + e0]);
+      v1 = __fadd_rn(v1, ex.bv[g * hs + e1]);
+    }
+    qh[e0] = __fsub_rn(__fmul_rn(q0, fcr), __fmul_rn(q1, fci));
+    qh[e1] = __fadd_rn(__fmul_rn(q0, fci), __fmul_rn(q1, fcr));
     const float r0 = __fsub_rn(__fmul_rn(k0, fcr), __fmul_rn(k1, fci));
     const float r1 = __fadd_rn(__fmul_rn(k0, fci), __fmul_rn(k1, fcr));
-    kh[2 * p] = r0;
-    kh[2 * p + 1] = r1;
-    vh[2 * p] = v[g * hs + 2 * p];
-    vh[2 * p + 1] = v[g * hs + 2 * p + 1];
+    kh[e0] = r0;
+    kh[e1] = r1;
+    vh[e0] = v0;
+    vh[e1] = v1;
     if (h % kv_mul == 0) {
-      kc[off + g * hs + 2 * p] = r0;
-      kc[off + g * hs + 2 * p + 1] = r1;
-      vc[off + g * hs + 2 * p] = vh[2 * p];
-      vc[off + g * hs + 2 * p + 1] = vh[2 * p + 1];
+      kc[off + g * hs + e0] = r0;
+      kc[off + g * hs + e1] = r1;
+      vc[off + g * hs + e0] = v0;
+      vc[off + g * hs + e1] = v1;
     }
   }
   sync();

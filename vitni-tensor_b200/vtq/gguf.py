@@ -131,24 +131,32 @@ MODEL_ID = "vitni-b200-synthetic-tinyllama"
 
 
 def synthetic_llama(cfg: dict = TINYLLAMA, seed: int = 0, embd_dtype: int = Q4_K,
-                    shared_head: bool = False) -> bytes:
+                    shared_head: bool = False, arch: str = "llama",
+                    qkv_bias: bool = False, wdtypes: dict = None) -> bytes:
     """Deterministic GGUF for BASELINE config 4: attention/FFN-gate/up weights
-    Q4_K, V / down / output head Q6_K, token_embd Q4_K, norms F32 = 1 + N(0, 0.02)."""
+    Q4_K, V / down / output head Q6_K, token_embd Q4_K, norms F32 = 1 + N(0, 0.02).
+    arch="qwen2" writes the Qwen2 keys (the reference then uses NeoX RoPE,
+    quant_weights.rs:151); qkv_bias adds F32 attn_q/k/v biases ~ N(0, 0.1);
+    wdtypes overrides the format per role (attn_q, attn_k, attn_v, attn_output,
+    ffn_gate, ffn_up, ffn_down, output), e.g. Q5_0 / Q8_0 as in Qwen2.5 files."""
+    dt = {"attn_q": Q4_K, "attn_k": Q4_K, "attn_v": Q6_K, "attn_output": Q4_K,
+          "ffn_gate": Q4_K, "ffn_up": Q4_K, "ffn_down": Q6_K, "output": Q6_K}
+    dt.update(wdtypes or {})
     d, h, L = cfg["dim"], cfg["hidden"], cfg["layers"]
     hs = d // cfg["heads"]
     kv = cfg["kv_heads"] * hs
     meta = [
-        ("general.architecture", STRING, "llama"),
+        ("general.architecture", STRING, arch),
         ("general.alignment", U32, 32),
-        ("llama.embedding_length", U32, d),
-        ("llama.feed_forward_length", U32, h),
-        ("llama.block_count", U32, L),
-        ("llama.attention.head_count", U32, cfg["heads"]),
-        ("llama.attention.head_count_kv", U32, cfg["kv_heads"]),
-        ("llama.context_length", U32, cfg["seq_len"]),
-        ("llama.vocab_size", U32, cfg["vocab"]),
-        ("llama.rope.freq_base", F32V, float(cfg["rope_theta"])),
-        ("llama.attention.layer_norm_rms_epsilon", F32V, float(cfg["rms_eps"])),
+        (f"{arch}.embedding_length", U32, d),
+        (f"{arch}.feed_forward_length", U32, h),
+        (f"{arch}.block_count", U32, L),
+        (f"{arch}.attention.head_count", U32, cfg["heads"]),
+        (f"{arch}.attention.head_count_kv", U32, cfg["kv_heads"]),
+        (f"{arch}.context_length", U32, cfg["seq_len"]),
+        (f"{arch}.vocab_size", U32, cfg["vocab"]),
+        (f"{arch}.rope.freq_base", F32V, float(cfg["rope_theta"])),
+        (f"{arch}.attention.layer_norm_rms_epsilon", F32V, float(cfg["rms_eps"])),
     ]
     tensors = []
 
@@ -163,17 +171,21 @@ def synthetic_llama(cfg: dict = TINYLLAMA, seed: int = 0, embd_dtype: int = Q4_K
     mat("token_embd.weight", embd_dtype, cfg["vocab"], d)
     for l in range(L):
         norm(f"blk.{l}.attn_norm.weight", d)
-        mat(f"blk.{l}.attn_q.weight", Q4_K, d, d)
-        mat(f"blk.{l}.attn_k.weight", Q4_K, kv, d)
-        mat(f"blk.{l}.attn_v.weight", Q6_K, kv, d)
-        mat(f"blk.{l}.attn_output.weight", Q4_K, d, d)
+        mat(f"blk.{l}.attn_q.weight", dt["attn_q"], d, d)
+        mat(f"blk.{l}.attn_k.weight", dt["attn_k"], kv, d)
+        mat(f"blk.{l}.attn_v.weight", dt["attn_v"], kv, d)
+        if qkv_bias:
+            for nm, n in (("attn_q", d), ("attn_k", kv), ("attn_v", kv)):
+                b = synth.normal(f"c4/{seed}/blk.{l}.{nm}.bias", seed, n) * np.float32(0.1)
+                tensors.append((f"blk.{l}.{nm}.bias", [n], F32, b.astype(np.float32).tobytes()))
+        mat(f"blk.{l}.attn_output.weight", dt["attn_output"], d, d)
         norm(f"blk.{l}.ffn_norm.weight", d)
-        mat(f"blk.{l}.ffn_gate.weight", Q4_K, h, d)
-        mat(f"blk.{l}.ffn_up.weight", Q4_K, h, d)
-        mat(f"blk.{l}.ffn_down.weight", Q6_K, d, h)
+        mat(f"blk.{l}.ffn_gate.weight", dt["ffn_gate"], h, d)
+        mat(f"blk.{l}.ffn_up.weight", dt["ffn_up"], h, d)
+        mat(f"blk.{l}.ffn_down.weight", dt["ffn_down"], d, h)
     norm("output_norm.weight", d)
     if not shared_head:
-        mat("output.weight", Q6_K, cfg["vocab"], d)
+        mat("output.weight", dt["output"], cfg["vocab"], d)
     return write(meta, tensors)
 
 
