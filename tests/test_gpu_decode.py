@@ -14,14 +14,17 @@ SMALL = dict(dim=256, hidden=512, layers=2, heads=4, kv_heads=2, vocab=300, seq_
              rope_theta=10000.0, rms_eps=1e-5)
 
 
+# (environment, expected vtq_decode_step_kind). Every path batches the prompt
+# positions except "no_prefill", which runs them one token at a time.
 STEP_PATHS = {"graph": ({}, 1), "persistent": ({"VTQ_DECODE_PERSISTENT": "1"}, 2),
-              "unfused": ({"VTQ_DECODE_UNFUSED": "1"}, 0)}
+              "unfused": ({"VTQ_DECODE_UNFUSED": "1"}, 0),
+              "no_prefill": ({"VTQ_DECODE_NO_PREFILL": "1"}, 1)}
 
 
 @pytest.fixture(params=list(STEP_PATHS))
 def step_path(request, monkeypatch):
     env, kind = STEP_PATHS[request.param]
-    for k in ("VTQ_DECODE_PERSISTENT", "VTQ_DECODE_UNFUSED"):
+    for k in ("VTQ_DECODE_PERSISTENT", "VTQ_DECODE_UNFUSED", "VTQ_DECODE_NO_PREFILL"):
         monkeypatch.delenv(k, raising=False)
     for k, v in env.items():
         monkeypatch.setenv(k, v)
@@ -45,7 +48,7 @@ def assert_bits(a, b):
 
 
 @pytest.mark.parametrize("variant", ["q4k_embd", "q6k_embd", "shared_head", "mha", "qwen2",
-                                     "qwen2_q5"])
+                                     "qwen2_q5", "long_prompt"])
 def test_small_models_bit_exact(variant, step_path):
     cfg = dict(SMALL)
     kw = {}
@@ -68,9 +71,12 @@ def test_small_models_bit_exact(variant, step_path):
                          "ffn_down": vtq.Q8_0}
         kw["embd_dtype"] = vtq.Q8_0
         kind = 0
+    n_prompt, n_new = 7, 9
+    if variant == "long_prompt":  # 20 batched prompt rows: Q4_K linears on the GEMM
+        n_prompt, n_new = 21, 4
     blob = gguf.synthetic_llama(cfg, seed=3, **kw)
-    prompt = gguf.prompt_tokens(7, cfg["vocab"], seed=1)
-    got, lg, again, ref, rlg = run_both(blob, prompt, 9, kind)
+    prompt = gguf.prompt_tokens(n_prompt, cfg["vocab"], seed=1)
+    got, lg, again, ref, rlg = run_both(blob, prompt, n_new, kind)
     assert_bits(lg, rlg)
     assert got == ref and again == ref
 

@@ -262,6 +262,7 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(float* x, const float* del
 
 // RMSNorm with the residual add written to a separate buffer:
 // v = x (+ delta) -> res; out = (v * scale) * w (rms_norm.rs:94-108).
+// Row blockIdx.x of [rows][n] buffers (one row in the decode step).
 __global__ void __launch_bounds__(256) rmsnorm_res_kernel(const float* x, const float* delta,
                                                           const float* w, float eps, int n,
                                                           float* out, float* res) {
@@ -270,6 +271,11 @@ __global__ void __launch_bounds__(256) rmsnorm_res_kernel(const float* x, const 
   __shared__ xsum::Scratch scr;
   pdl_wait();
   pdl_release();
+  const size_t row = (size_t)blockIdx.x * n;
+  x += row;
+  if (delta) delta += row;
+  out += row;
+  res += row;
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
     float v = x[i];
     if (delta) v = __fadd_rn(v, delta[i]);
@@ -287,6 +293,74 @@ __global__ void __launch_bounds__(256) rmsnorm_res_kernel(const float* x, const 
   const float scale = s_scale;
   for (int i = threadIdx.x; i < n; i += blockDim.x)
     out[i] = __fmul_rn(__fmul_rn(res[i], scale), w[i]);
+}
+
+// ---- batched prompt (positions 0 .. P-1 of the prompt at once) ----
+
+// Embedding rows of the prompt tokens: row blockIdx.y.
+__global__ void embed_rows_kernel(const uint8_t* table, int dtype, int64_t pitch, int dim,
+                                  const uint32_t* tokens, float* x) {
+  const uint32_t row = tokens[blockIdx.y];
+  float* xr = x + (size_t)blockIdx.y * dim;
+  for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < dim; e += gridDim.x * blockDim.x)
+    xr[e] = embed_value(table, dtype, pitch, dim, row, e);
+}
+
+// k (+ bias) rotated and v (+ bias) into the caches at position blockIdx.x, with
+// the arithmetic of attention_head (decode_ops.cuh), for every kv head.
+__global__ void cache_kv_rows_kernel(const float* k, int64_t ldk, const float* v, int64_t ldv,
+                                     AttnExtras ex, float* kc, float* vc, int layer,
+                                     int seq_len, int kv_dim, int hs, const float* rcos,
+                                     const float* rsin) {
+  const int pos = blockIdx.x, half = hs / 2;
+  const float* kr = k + (size_t)pos * ldk;
+  const float* vr = v + (size_t)pos * ldv;
+  const size_t off = ((size_t)layer * seq_len + pos) * kv_dim;
+  for (int idx = threadIdx.x; idx < kv_dim / 2; idx += blockDim.x) {
+    const int g = idx / half, p = idx - g * half;
+    const int e0 = ex.neox ? p : 2 * p, e1 = ex.neox ? p + half : 2 * p + 1;
+    const float fcr = rcos[(size_t)pos * half + p], fci = rsin[(size_t)pos * half + p];
+    float k0 = kr[g * hs + e0], k1 = kr[g * hs + e1];
+    float v0 = vr[g * hs + e0], v1 = vr[g * hs + e1];
+    if (ex.bk) {
+      k0 = __fadd_rn(k0, ex.bk[g * hs + e0]);
+      k1 = __fadd_rn(k1, ex.bk[g * hs + e1]);
+    }
+    if (ex.bv) {
+      v0 = __fadd_rn(v0, ex.bv[g * hs + e0]);
+      v1 = __fadd_rn(v1, ex.bv[g * hs + e1]);
+    }
+    kc[off + g * hs + e0] = __fsub_rn(__fmul_rn(k0, fcr), __fmul_rn(k1, fci));
+    kc[off + g * hs + e1] = __fadd_rn(__fmul_rn(k0, fci), __fmul_rn(k1, fcr));
+    vc[off + g * hs + e0] = v0;
+    vc[off + g * hs + e1] = v1;
+  }
+}
+
+// Attention of head blockIdx.x for prompt position blockIdx.y over the cache
+// (every prompt position's k / v is cached before this launch).
+__global__ void attention_rows_kernel(const float* q, int64_t ldq, const float* k, const float* v,
+                                      int64_t ldv, float* kc, float* vc, int layer, int seq_len,
+                                      int kv_dim, int hs, int kv_mul, const float* rcos,
+                                      const float* rsin, float* out, int dim, AttnExtras ex) {
+  extern __shared__ float sm[];
+  __shared__ float red[2];
+  const int t = blockIdx.y;
+  ex.no_cache_write = 1;
+  attention_head(blockIdx.x, q + (size_t)t * ldq, k + (size_t)t * ldq, v + (size_t)t * ldv, kc,
+                 vc, layer, seq_len, kv_dim, hs, kv_mul, rcos, rsin, t, out + (size_t)t * dim, sm,
+                 red, threadIdx.x, blockDim.x, [] { __syncthreads(); }, ex);
+}
+
+// SwiGLU of prompt row blockIdx.y: g / u read with stride st from rows of ld.
+__global__ void swiglu_rows_kernel(const float* g, const float* u, int st, int64_t ld,
+                                   float* out, int n) {
+  const size_t r = blockIdx.y;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const float gi = g[r * ld + (int64_t)i * st];
+    const float silu = __fdiv_rn(gi, __fadd_rn(1.0f, libm::expf(-gi)));
+    out[r * n + i] = __fmul_rn(silu, u[r * ld + (int64_t)i * st]);
+  }
 }
 
 // One query head per CTA (attention_head, decode_ops.cuh).
@@ -379,6 +453,13 @@ struct vtq_decode {
   cudaStream_t side = nullptr;
   cudaEvent_t fork = nullptr, join = nullptr;
   float ms_steps = 0.0f, ms_call = 0.0f;
+  // Batched prompt: positions 0 .. n_prompt-2 run as batched linears before the
+  // per-token loop (their next token is the prompt's, so only the KV cache and
+  // the logged logits carry over). Row buffers for up to pf_cap positions.
+  bool prefill = true;
+  int pf_cap = 0;
+  float *pf_x = nullptr, *pf_xr = nullptr, *pf_xb = nullptr, *pf_q = nullptr, *pf_v = nullptr,
+        *pf_xo = nullptr, *pf_xb2 = nullptr, *pf_g = nullptr, *pf_inner = nullptr;
   std::string err;
 };
 
@@ -800,6 +881,7 @@ vtq_status vtq_decode_open(vtq_ctx* ctx, int device, const uint8_t* gguf, size_t
   d->fused = kq(d->head) && dim % 256 == 0 && d->hidden % 256 == 0 && dim * 4 <= 65536 &&
              d->hidden * 4 <= 65536 && getenv("VTQ_DECODE_UNFUSED") == nullptr;
   if (const char* e = getenv("VTQ_DECODE_FUSE")) d->fuse_mask = atoi(e) & 3;
+  d->prefill = getenv("VTQ_DECODE_NO_PREFILL") == nullptr;
   for (auto& L : d->layers)
     d->fused = d->fused && L.fused_qk && L.fused_13 && kq(L.wqk) && kq(L.wv) && kq(L.wo) &&
                kq(L.w13) && kq(L.w2);
@@ -858,6 +940,82 @@ vtq_status vtq_decode_config(const vtq_decode* d, int64_t* out8) {
   return VTQ_OK;
 }
 
+// Batched prompt positions 0 .. P-1 (forward_quantized.rs:329-649 per position,
+// run as batched linears): every linear produces, row by row, the bits of the
+// per-position call (the batch rows are independent: quant.rs:936-980), the
+// norms and SwiGLU are per row, and each position's attention reads the cache
+// exactly as the per-token step does once keys / values of positions <= it
+// are cached. Fills the KV cache and, with want_logits, rows 0 .. P-1 of the
+// logits log; the per-token loop then starts at position P.
+vtq_status enqueue_prefill(vtq_decode* d, int P, bool want_logits) {
+  cudaStream_t s = d->stream;
+  const int dim = d->dim, hs = dim / d->n_heads, kv_dim = d->n_kv_heads * hs, H = d->hidden;
+  const int kv_mul = d->n_heads / d->n_kv_heads;
+  const int64_t ldqk = dim + kv_dim;
+  if (P > d->pf_cap) {
+    const int cap = std::min(d->seq_len, std::max(P, 2 * d->pf_cap));
+    const size_t c = (size_t)cap;
+    for (auto pr : {std::make_pair(&d->pf_x, c * dim), std::make_pair(&d->pf_xr, c * dim),
+                    std::make_pair(&d->pf_xb, c * dim), std::make_pair(&d->pf_q, c * ldqk),
+                    std::make_pair(&d->pf_v, c * kv_dim), std::make_pair(&d->pf_xo, c * dim),
+                    std::make_pair(&d->pf_xb2, c * dim), std::make_pair(&d->pf_g, c * 2 * H),
+                    std::make_pair(&d->pf_inner, c * H)})
+      if (vtq_status e = dalloc(d, pr.first, pr.second * 4)) return e;
+    d->pf_cap = cap;
+  }
+  const size_t rms_smem = ((size_t)dim + 4) * 4;
+  const size_t att_smem = ((size_t)3 * hs + d->seq_len) * 4;
+  if (att_smem > 48 * 1024)
+    DCUDA(d, cudaFuncSetAttribute(attention_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)att_smem));
+  auto lin = [&](const DevMatrix& m, const float* x, int64_t ldx, float* y, int64_t ldy) {
+    return linear_any(m, x, ldx, y, ldy, P, d->status, s);
+  };
+  float *A = d->pf_x, *B = d->pf_xr;
+  embed_rows_kernel<<<dim3((dim + 255) / 256, P), 256, 0, s>>>(d->embd.data, d->embd.dtype,
+                                                                d->embd.pitch, dim, d->prompt, A);
+  const float* delta = nullptr;
+  for (int l = 0; l < d->n_layers; l++) {
+    auto& L = d->layers[l];
+    rmsnorm_res_kernel<<<P, 256, rms_smem, s>>>(A, delta, L.rms_att, d->rms_eps, dim, d->pf_xb, B);
+    if (L.fused_qk) {
+      DCUDA(d, lin(L.wqk, d->pf_xb, dim, d->pf_q, ldqk));
+    } else {
+      DCUDA(d, lin(L.wq, d->pf_xb, dim, d->pf_q, ldqk));
+      DCUDA(d, lin(L.wk, d->pf_xb, dim, d->pf_q + dim, ldqk));
+    }
+    DCUDA(d, lin(L.wv, d->pf_xb, dim, d->pf_v, kv_dim));
+    const AttnExtras ex{d->neox ? 1 : 0, L.bq, L.bk, L.bv};
+    cache_kv_rows_kernel<<<P, 128, 0, s>>>(d->pf_q + dim, ldqk, d->pf_v, kv_dim, ex, d->kc, d->vc,
+                                           l, d->seq_len, kv_dim, hs, d->rcos, d->rsin);
+    attention_rows_kernel<<<dim3(d->n_heads, P), 128, att_smem, s>>>(
+        d->pf_q, ldqk, d->pf_q + dim, d->pf_v, kv_dim, d->kc, d->vc, l, d->seq_len, kv_dim, hs,
+        kv_mul, d->rcos, d->rsin, d->pf_xo, dim, ex);
+    DCUDA(d, lin(L.wo, d->pf_xo, dim, d->pf_xb2, dim));
+    rmsnorm_res_kernel<<<P, 256, rms_smem, s>>>(B, d->pf_xb2, L.rms_ffn, d->rms_eps, dim,
+                                                d->pf_xb, A);
+    if (L.fused_13) {  // rows interleaved (gate_i, up_i)
+      DCUDA(d, lin(L.w13, d->pf_xb, dim, d->pf_g, 2 * H));
+      swiglu_rows_kernel<<<dim3((H + 255) / 256, P), 256, 0, s>>>(d->pf_g, d->pf_g + 1, 2, 2 * H,
+                                                                   d->pf_inner, H);
+    } else {
+      DCUDA(d, lin(L.w1, d->pf_xb, dim, d->pf_g, 2 * H));
+      DCUDA(d, lin(L.w3, d->pf_xb, dim, d->pf_g + H, 2 * H));
+      swiglu_rows_kernel<<<dim3((H + 255) / 256, P), 256, 0, s>>>(d->pf_g, d->pf_g + H, 1, 2 * H,
+                                                                   d->pf_inner, H);
+    }
+    DCUDA(d, lin(L.w2, d->pf_inner, H, d->pf_xb2, dim));
+    delta = d->pf_xb2;
+  }
+  if (want_logits) {
+    rmsnorm_res_kernel<<<P, 256, rms_smem, s>>>(A, delta, d->rms_final, d->rms_eps, dim,
+                                                d->pf_xb, B);
+    DCUDA(d, lin(d->head, d->pf_xb, dim, d->logit_log, d->vocab));
+  }
+  DCUDA(d, cudaGetLastError());
+  return VTQ_OK;
+}
+
 vtq_status vtq_decode_run(vtq_decode* d, const uint32_t* prompt, size_t n_prompt, size_t n_new,
                           uint32_t* out_tokens, float* logits) {
   if (!d || (!prompt && n_prompt) || (!out_tokens && n_new)) return VTQ_ERR_INVALID_ARG;
@@ -881,16 +1039,20 @@ vtq_status vtq_decode_run(vtq_decode* d, const uint32_t* prompt, size_t n_prompt
       d->graph = nullptr;
     }
   }
+  // Prompt positions whose next token is the prompt's own run batched.
+  const size_t P0 = d->prefill && n_prompt >= 2 ? n_prompt - 1 : 0;
   if (d->mk) {
     // Persistent step kernel: one cooperative launch per position.
     if (!d->ev[0])
       for (auto& e : d->ev) DCUDA(d, cudaEventCreate(&e));
     DCUDA(d, cudaEventRecord(d->ev[0], d->stream));
-    StepState hs0{0, prompt[0], (int)n_prompt, (int)total, 0};
+    StepState hs0{(int)P0, prompt[P0], (int)n_prompt, (int)total, 0};
     DCUDA(d, cudaMemcpyAsync(d->st, &hs0, sizeof hs0, cudaMemcpyHostToDevice, d->stream));
     DCUDA(d, cudaMemcpyAsync(d->prompt, prompt, n_prompt * 4, cudaMemcpyHostToDevice, d->stream));
     DCUDA(d, cudaEventRecord(d->ev[1], d->stream));
-    for (size_t pos = 0; pos < total; pos++)
+    if (P0 > 0)
+      if (vtq_status e = enqueue_prefill(d, (int)P0, want_logits)) return e;
+    for (size_t pos = P0; pos < total; pos++)
       DCUDA(d, mk_launch(d->mk, want_logits ? d->logit_log : nullptr, d->stream));
     DCUDA(d, cudaEventRecord(d->ev[2], d->stream));
     if (n_new)
@@ -931,11 +1093,13 @@ vtq_status vtq_decode_run(vtq_decode* d, const uint32_t* prompt, size_t n_prompt
   if (!d->ev[0])
     for (auto& e : d->ev) DCUDA(d, cudaEventCreate(&e));
   DCUDA(d, cudaEventRecord(d->ev[0], d->stream));
-  StepState hs{0, prompt[0], (int)n_prompt, (int)total, 0};
+  StepState hs{(int)P0, prompt[P0], (int)n_prompt, (int)total, 0};
   DCUDA(d, cudaMemcpyAsync(d->st, &hs, sizeof hs, cudaMemcpyHostToDevice, d->stream));
   DCUDA(d, cudaMemcpyAsync(d->prompt, prompt, n_prompt * 4, cudaMemcpyHostToDevice, d->stream));
   DCUDA(d, cudaEventRecord(d->ev[1], d->stream));
-  for (size_t pos = 0; pos < total; pos++) DCUDA(d, cudaGraphLaunch(d->graph, d->stream));
+  if (P0 > 0)
+    if (vtq_status e = enqueue_prefill(d, (int)P0, want_logits)) return e;
+  for (size_t pos = P0; pos < total; pos++) DCUDA(d, cudaGraphLaunch(d->graph, d->stream));
   DCUDA(d, cudaEventRecord(d->ev[2], d->stream));
   if (n_new)
     DCUDA(d, cudaMemcpyAsync(out_tokens, d->out_tokens, n_new * 4, cudaMemcpyDeviceToHost,

@@ -17,6 +17,7 @@ namespace {
 struct AttnExtras {
   int neox;
   const float *bq, *bk, *bv;
+  int no_cache_write = 0;  // batched prompt: k / v already cached for every position
 };
 
 // embedding_row (forward_quantized.rs:818-919): element e of row `row` of the
@@ -118,7 +119,7 @@ __device__ __forceinline__ void attention_head(int h, const float* q, const floa
     kh[e1] = r1;
     vh[e0] = v0;
     vh[e1] = v1;
-    if (h % kv_mul == 0) {
+    if (h % kv_mul == 0 && !ex.no_cache_write) {
       kc[off + g * hs + e0] = r0;
       kc[off + g * hs + e1] = r1;
       vc[off + g * hs + e0] = v0;

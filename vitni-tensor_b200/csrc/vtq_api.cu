@@ -258,6 +258,13 @@ vtq_status check_kquant(vtq_ctx* c, const char* fn, int bytes_per_sb, size_t wle
 
 }  // namespace
 
+namespace vtq {
+cudaError_t linear_any(const DevMatrix& m, const float* x, int64_t ldx, float* y, int64_t ldy,
+                       int64_t batch, unsigned* status, cudaStream_t st) {
+  return run_linear(m, x, ldx, y, ldy, batch, 0, status, st);
+}
+}  // namespace vtq
+
 extern "C" {
 
 vtq_status vtq_init(int device, vtq_ctx** out) {

@@ -96,6 +96,11 @@ cudaError_t launch_canon_matvec(const DevMatrix& m, const float* x, int64_t ldx,
                                 float* y, int64_t ldy, unsigned* status, cudaStream_t st);
 
 // The linear_dispatch arm for m's dtype (integer k-quant or canonical), batch 1.
+// A linear of any device format over `batch` activation rows, dispatched like
+// vtq_linear: the tcgen05 GEMM for Q4_K at batch >= 16, the integer matvec for
+// Q4_K / Q6_K, the canonical fp32 kernel otherwise.
+cudaError_t linear_any(const DevMatrix& m, const float* x, int64_t ldx, float* y, int64_t ldy,
+                       int64_t batch, unsigned* status, cudaStream_t st);
 cudaError_t launch_kq_or_canon(const DevMatrix& m, const float* x, float* y, unsigned* status,
                                cudaStream_t st);
 
