@@ -173,6 +173,10 @@ vtq_status vtq_decode_debug_buffer(vtq_decode* d, int which, float* out, size_t 
  * the model fits it), VTQ_DECODE_UNFUSED (per-op kernels without the fused
  * norm). No reference counterpart. */
 int vtq_decode_step_kind(const vtq_decode* d);
+/* Kernels this library launched for the last vtq_decode_run's decode work (the
+ * batched prompt's launches plus the step graph's kernel nodes per step, or one
+ * per step for the persistent kernel). No reference counterpart. */
+unsigned long long vtq_decode_launches(const vtq_decode* d);
 vtq_status vtq_decode_close(vtq_decode* d);
 
 /* ---- The left-to-right fp32 sum of non-negative terms (the sum of squares of

@@ -350,6 +350,7 @@ cudaError_t launch_fmt(const CUtensorMap& tm, const CnParams& p, int grid, uint3
     if (e != cudaSuccess) return e;
     attr_set = true;
   }
+  kernel_launch_count()++;
   canon_matvec_kernel<FMT, MAXB><<<grid, CN_THREADS, smem, st>>>(tm, p);
   return cudaGetLastError();
 }

@@ -458,6 +458,8 @@ struct vtq_decode {
   // the logged logits carry over). Row buffers for up to pf_cap positions.
   bool prefill = true;
   int pf_cap = 0;
+  unsigned long long launches = 0;  // kernels of the last vtq_decode_run's decode work
+  unsigned long long graph_kernels = 0;  // kernel nodes of the step graph
   float *pf_x = nullptr, *pf_xr = nullptr, *pf_xb = nullptr, *pf_q = nullptr, *pf_v = nullptr,
         *pf_xo = nullptr, *pf_xb2 = nullptr, *pf_g = nullptr, *pf_inner = nullptr;
   std::string err;
@@ -927,6 +929,8 @@ vtq_status vtq_decode_open(vtq_ctx* ctx, int device, const uint8_t* gguf, size_t
 
 const char* vtq_decode_last_error(const vtq_decode* d) { return d ? d->err.c_str() : "null"; }
 
+unsigned long long vtq_decode_launches(const vtq_decode* d) { return d ? d->launches : 0; }
+
 int vtq_decode_step_kind(const vtq_decode* d) {
   if (!d) return -1;
   return d->mk ? 2 : d->fused ? 1 : 0;
@@ -971,12 +975,15 @@ vtq_status enqueue_prefill(vtq_decode* d, int P, bool want_logits) {
   auto lin = [&](const DevMatrix& m, const float* x, int64_t ldx, float* y, int64_t ldy) {
     return linear_any(m, x, ldx, y, ldy, P, d->status, s);
   };
+  unsigned long long& count = kernel_launch_count();
   float *A = d->pf_x, *B = d->pf_xr;
+  count++;
   embed_rows_kernel<<<dim3((dim + 255) / 256, P), 256, 0, s>>>(d->embd.data, d->embd.dtype,
                                                                 d->embd.pitch, dim, d->prompt, A);
   const float* delta = nullptr;
   for (int l = 0; l < d->n_layers; l++) {
     auto& L = d->layers[l];
+    count++;
     rmsnorm_res_kernel<<<P, 256, rms_smem, s>>>(A, delta, L.rms_att, d->rms_eps, dim, d->pf_xb, B);
     if (L.fused_qk) {
       DCUDA(d, lin(L.wqk, d->pf_xb, dim, d->pf_q, ldqk));
@@ -986,21 +993,26 @@ vtq_status enqueue_prefill(vtq_decode* d, int P, bool want_logits) {
     }
     DCUDA(d, lin(L.wv, d->pf_xb, dim, d->pf_v, kv_dim));
     const AttnExtras ex{d->neox ? 1 : 0, L.bq, L.bk, L.bv};
+    count++;
     cache_kv_rows_kernel<<<P, 128, 0, s>>>(d->pf_q + dim, ldqk, d->pf_v, kv_dim, ex, d->kc, d->vc,
                                            l, d->seq_len, kv_dim, hs, d->rcos, d->rsin);
+    count++;
     attention_rows_kernel<<<dim3(d->n_heads, P), 128, att_smem, s>>>(
         d->pf_q, ldqk, d->pf_q + dim, d->pf_v, kv_dim, d->kc, d->vc, l, d->seq_len, kv_dim, hs,
         kv_mul, d->rcos, d->rsin, d->pf_xo, dim, ex);
     DCUDA(d, lin(L.wo, d->pf_xo, dim, d->pf_xb2, dim));
+    count++;
     rmsnorm_res_kernel<<<P, 256, rms_smem, s>>>(B, d->pf_xb2, L.rms_ffn, d->rms_eps, dim,
                                                 d->pf_xb, A);
     if (L.fused_13) {  // rows interleaved (gate_i, up_i)
       DCUDA(d, lin(L.w13, d->pf_xb, dim, d->pf_g, 2 * H));
+      count++;
       swiglu_rows_kernel<<<dim3((H + 255) / 256, P), 256, 0, s>>>(d->pf_g, d->pf_g + 1, 2, 2 * H,
                                                                    d->pf_inner, H);
     } else {
       DCUDA(d, lin(L.w1, d->pf_xb, dim, d->pf_g, 2 * H));
       DCUDA(d, lin(L.w3, d->pf_xb, dim, d->pf_g + H, 2 * H));
+      count++;
       swiglu_rows_kernel<<<dim3((H + 255) / 256, P), 256, 0, s>>>(d->pf_g, d->pf_g + H, 1, 2 * H,
                                                                    d->pf_inner, H);
     }
@@ -1008,6 +1020,7 @@ vtq_status enqueue_prefill(vtq_decode* d, int P, bool want_logits) {
     delta = d->pf_xb2;
   }
   if (want_logits) {
+    count++;
     rmsnorm_res_kernel<<<P, 256, rms_smem, s>>>(A, delta, d->rms_final, d->rms_eps, dim,
                                                 d->pf_xb, B);
     DCUDA(d, lin(d->head, d->pf_xb, dim, d->logit_log, d->vocab));
@@ -1050,10 +1063,12 @@ vtq_status vtq_decode_run(vtq_decode* d, const uint32_t* prompt, size_t n_prompt
     DCUDA(d, cudaMemcpyAsync(d->st, &hs0, sizeof hs0, cudaMemcpyHostToDevice, d->stream));
     DCUDA(d, cudaMemcpyAsync(d->prompt, prompt, n_prompt * 4, cudaMemcpyHostToDevice, d->stream));
     DCUDA(d, cudaEventRecord(d->ev[1], d->stream));
+    const unsigned long long c0 = kernel_launch_count();
     if (P0 > 0)
       if (vtq_status e = enqueue_prefill(d, (int)P0, want_logits)) return e;
     for (size_t pos = P0; pos < total; pos++)
       DCUDA(d, mk_launch(d->mk, want_logits ? d->logit_log : nullptr, d->stream));
+    d->launches = kernel_launch_count() - c0 + (total - P0);
     DCUDA(d, cudaEventRecord(d->ev[2], d->stream));
     if (n_new)
       DCUDA(d, cudaMemcpyAsync(out_tokens, d->out_tokens, n_new * 4, cudaMemcpyDeviceToHost,
@@ -1087,6 +1102,16 @@ vtq_status vtq_decode_run(vtq_decode* d, const uint32_t* prompt, size_t n_prompt
     if (s) return s;
     DCUDA(d, ce);
     DCUDA(d, cudaGraphInstantiate(&d->graph, graph, 0));
+    size_t nn = 0;
+    DCUDA(d, cudaGraphGetNodes(graph, nullptr, &nn));
+    std::vector<cudaGraphNode_t> nodes(nn);
+    DCUDA(d, cudaGraphGetNodes(graph, nodes.data(), &nn));
+    d->graph_kernels = 0;
+    for (auto nd : nodes) {
+      cudaGraphNodeType t;
+      DCUDA(d, cudaGraphNodeGetType(nd, &t));
+      d->graph_kernels += t == cudaGraphNodeTypeKernel;
+    }
     cudaGraphDestroy(graph);
     d->graph_logs = want_logits;
   }
@@ -1097,9 +1122,11 @@ vtq_status vtq_decode_run(vtq_decode* d, const uint32_t* prompt, size_t n_prompt
   DCUDA(d, cudaMemcpyAsync(d->st, &hs, sizeof hs, cudaMemcpyHostToDevice, d->stream));
   DCUDA(d, cudaMemcpyAsync(d->prompt, prompt, n_prompt * 4, cudaMemcpyHostToDevice, d->stream));
   DCUDA(d, cudaEventRecord(d->ev[1], d->stream));
+  const unsigned long long c0 = kernel_launch_count();
   if (P0 > 0)
     if (vtq_status e = enqueue_prefill(d, (int)P0, want_logits)) return e;
   for (size_t pos = P0; pos < total; pos++) DCUDA(d, cudaGraphLaunch(d->graph, d->stream));
+  d->launches = kernel_launch_count() - c0 + d->graph_kernels * (total - P0);
   DCUDA(d, cudaEventRecord(d->ev[2], d->stream));
   if (n_new)
     DCUDA(d, cudaMemcpyAsync(out_tokens, d->out_tokens, n_new * 4, cudaMemcpyDeviceToHost,

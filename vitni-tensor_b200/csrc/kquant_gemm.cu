@@ -550,6 +550,7 @@ cudaError_t launch_lv(const CUtensorMap& tmx, const CUtensorMap& tmw, const Gemm
     if (e != cudaSuccess) return e;
     attr = true;
   }
+  kernel_launch_count()++;
   kq_gemm_kernel<LV><<<grid, kThreads, SMEM_BYTES, st>>>(tmx, tmw, p);
   return cudaGetLastError();
 }
@@ -574,6 +575,7 @@ cudaError_t launch_kq_gemm(const DevMatrix& m, const float* x, int64_t ldx, int6
   float* xd = reinterpret_cast<float*>(buf + xq_bytes);
   {
     const int64_t blocks = ((int64_t)M * S + 7) / 8;
+    kernel_launch_count()++;
     quantize_rows_kernel<<<(unsigned)blocks, 256, 0, st>>>(x, ldx, M, n, xq, xd);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }

@@ -295,6 +295,7 @@ cudaError_t launch_variant(const KqParams& p, int grid, uint32_t smem, cudaStrea
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = use_pdl() ? 1 : 0;
+  kernel_launch_count()++;
   return cudaLaunchKernelEx(&cfg, kq_matvec_kernel<QT, MAXB, NCH, CW>, p);
 }
 

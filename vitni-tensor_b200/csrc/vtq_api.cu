@@ -259,6 +259,11 @@ vtq_status check_kquant(vtq_ctx* c, const char* fn, int bytes_per_sb, size_t wle
 }  // namespace
 
 namespace vtq {
+unsigned long long& kernel_launch_count() {
+  static thread_local unsigned long long n = 0;
+  return n;
+}
+
 cudaError_t linear_any(const DevMatrix& m, const float* x, int64_t ldx, float* y, int64_t ldy,
                        int64_t batch, unsigned* status, cudaStream_t st) {
   return run_linear(m, x, ldx, y, ldy, batch, 0, status, st);

@@ -96,6 +96,10 @@ cudaError_t launch_canon_matvec(const DevMatrix& m, const float* x, int64_t ldx,
                                 float* y, int64_t ldy, unsigned* status, cudaStream_t st);
 
 // The linear_dispatch arm for m's dtype (integer k-quant or canonical), batch 1.
+// Kernel launches issued by this library's linear launchers since load
+// (graph replays are not launches of the launcher; callers count those).
+unsigned long long& kernel_launch_count();
+
 // A linear of any device format over `batch` activation rows, dispatched like
 // vtq_linear: the tcgen05 GEMM for Q4_K at batch >= 16, the integer matvec for
 // Q4_K / Q6_K, the canonical fp32 kernel otherwise.

@@ -41,7 +41,7 @@ EXPORTS = (
     "vtq_gather_create", "vtq_gather_connect", "vtq_gather_y", "vtq_linear_gather",
     "vtq_gather_wait", "vtq_gather_destroy", "vtq_libm_sweep_device", "vtq_linear_gather_wait",
     "vtq_decode_timing", "vtq_decode_debug_buffer", "vtq_decode_step_kind",
-    "vtq_exact_sum_host", "vtq_exact_sum_device",
+    "vtq_exact_sum_host", "vtq_exact_sum_device", "vtq_decode_launches",
 )
 
 
@@ -132,6 +132,7 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         "vtq_libm_sweep": (None, [c_p, c_sz, c_p]),
         "vtq_decode_timing": (c_i32, [c_p, c_p]),
         "vtq_decode_step_kind": (c_i32, [c_p]),
+        "vtq_decode_launches": (ctypes.c_ulonglong, [c_p]),
         "vtq_exact_sum_host": (ctypes.c_float, [c_p, c_sz, c_p]),
         "vtq_exact_sum_device": (c_i32, [c_p, c_i32, c_i32, c_i32, c_p]),
         "vtq_decode_debug_buffer": (c_i32, [c_p, ctypes.c_int, c_p, c_sz]),
@@ -372,6 +373,10 @@ class DecodeSession:
         t = np.zeros(2, np.float32)
         self.lib.vtq_decode_timing(self.handle, _ptr(t))
         return float(t[0]), float(t[1])
+
+    def launches(self) -> int:
+        """Kernels launched for the last run's decode work (batched prompt + steps)."""
+        return int(self.lib.vtq_decode_launches(self.handle))
 
     def close(self):
         if getattr(self, "handle", None):
