@@ -38,7 +38,9 @@
 #include <cuda.h>
 #include <cuda_fp16.h>
 
+#include <map>
 #include <mutex>
+#include <vector>
 #include <unordered_map>
 
 #include "vtq_device.cuh"
@@ -510,30 +512,31 @@ cudaError_t byte_map(CUtensorMap* tm, const void* ptr, int64_t rows, int64_t col
              : cudaErrorInvalidValue;
 }
 
-// Per-device scratch for the quantised activations (grown on demand).
+// Scratch for the quantised activations, one buffer per (device, stream): GEMMs
+// on different streams never share it, and work on one stream is ordered. A
+// buffer that is outgrown is retired, not freed: launches already queued, and
+// CUDA graphs captured with it, keep a valid pointer (the retired buffers are
+// released at process exit).
 struct Scratch {
   uint8_t* ptr = nullptr;
   size_t cap = 0;
 };
 std::mutex g_scratch_mu;
-Scratch g_scratch[64];
+std::map<std::pair<int, cudaStream_t>, Scratch> g_scratch;
+std::vector<uint8_t*> g_scratch_retired;
 
-cudaError_t scratch(size_t bytes, uint8_t** out) {
+cudaError_t scratch(size_t bytes, cudaStream_t st, uint8_t** out) {
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (cudaGetDevice(&dev) != cudaSuccess) return cudaErrorInvalidDevice;
   std::lock_guard<std::mutex> lock(g_scratch_mu);
-  Scratch& sc = g_scratch[dev];
+  Scratch& sc = g_scratch[{dev, st}];
   if (sc.cap < bytes) {
-    if (sc.ptr) {
-      cudaError_t e = cudaDeviceSynchronize();
-      if (e != cudaSuccess) return e;
-      cudaFree(sc.ptr);
-      sc.ptr = nullptr;
-      sc.cap = 0;
-    }
     const size_t cap = (bytes + (1u << 20) - 1) & ~(size_t)((1u << 20) - 1);
-    cudaError_t e = cudaMalloc(&sc.ptr, cap);
+    uint8_t* p = nullptr;
+    cudaError_t e = cudaMalloc(&p, cap);
     if (e != cudaSuccess) return e;
+    if (sc.ptr) g_scratch_retired.push_back(sc.ptr);
+    sc.ptr = p;
     sc.cap = cap;
   }
   *out = sc.ptr;
@@ -569,7 +572,7 @@ cudaError_t launch_kq_gemm(const DevMatrix& m, const float* x, int64_t ldx, int6
   const int n = (int)m.in_feat, S = n / 256, M = (int)batch, R = (int)m.out_feat;
   const size_t xq_bytes = ((size_t)M * n + 1023) & ~(size_t)1023;
   uint8_t* buf = nullptr;
-  cudaError_t e = scratch(xq_bytes + (size_t)M * S * 4, &buf);
+  cudaError_t e = scratch(xq_bytes + (size_t)M * S * 4, st, &buf);
   if (e != cudaSuccess) return e;
   int8_t* xq = reinterpret_cast<int8_t*>(buf);
   float* xd = reinterpret_cast<float*>(buf + xq_bytes);
