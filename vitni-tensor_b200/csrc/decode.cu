@@ -884,6 +884,19 @@ vtq_status vtq_decode_open(vtq_ctx* ctx, int device, const uint8_t* gguf, size_t
              d->hidden * 4 <= 65536 && getenv("VTQ_DECODE_UNFUSED") == nullptr;
   if (const char* e = getenv("VTQ_DECODE_FUSE")) d->fuse_mask = atoi(e) & 3;
   d->prefill = getenv("VTQ_DECODE_NO_PREFILL") == nullptr;
+  // Attention keeps 3 head vectors and one score per cached position in shared
+  // memory: long contexts need the opt-in size.
+  {
+    const size_t att_smem = ((size_t)3 * hs + d->seq_len) * 4;
+    int optin = 0;
+    DCUDA(d, cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, d->device));
+    if (att_smem > (size_t)optin)
+      return dfail(d, VTQ_ERR_NOT_IMPLEMENTED,
+                   "decode session: context_length too long for the attention kernel");
+    if (att_smem > 48 * 1024)
+      DCUDA(d, cudaFuncSetAttribute(attention_rope_kernel,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, (int)att_smem));
+  }
   for (auto& L : d->layers)
     d->fused = d->fused && L.fused_qk && L.fused_13 && kq(L.wqk) && kq(L.wv) && kq(L.wo) &&
                kq(L.w13) && kq(L.w2);
