@@ -56,16 +56,16 @@ def peaks():
         return 6650.0, "fallback"
 
 
-def profile_traffic(cfg):
-    """dram bytes per launch of the dominant kernel from the committed ncu summary."""
-    path = os.path.join(REPO, "profiles", f"kq_matvec_{cfg}.md")
+def profile_traffic(cfg, mode):
+    """DRAM bytes (read + write) per launch of the dominant kernel, from one ncu
+    capture of the same launch (profiles/dram_traffic.json, machine-readable;
+    keyed by workload and launch mode). None when no capture exists."""
     try:
-        for line in open(path):
-            if line.startswith("dram_bytes_per_launch:"):
-                return float(line.split(":")[1])
-    except OSError:
-        pass
-    return None
+        with open(os.path.join(REPO, "profiles", "dram_traffic.json")) as f:
+            t = json.load(f).get(f"{cfg}/{mode}")
+        return None if t is None else float(t["dram_bytes_per_launch"])
+    except (OSError, ValueError, KeyError):
+        return None
 
 
 class ClockSampler:
@@ -188,12 +188,11 @@ def run_reference(args, world, rank):
     print(json.dumps(line), flush=True)
 
 
-def cpu_baseline(cfg_name, budget_s=12.0):
-    """Oracle timed on the host cores on a bounded sample of the workload."""
+def cpu_baseline(cfg_name, threads, budget_s=12.0):
+    """Oracle timed on `threads` host cores on a bounded sample of the workload."""
     from vtq import synth
     from oracle import oracle as O
     cfg = synth.CONFIGS[cfg_name]
-    threads = os.cpu_count() or 1
     mats = [(dt, n, r, synth.weight(dt, f"{cfg_name}.w.{n}x{r}", r, n),
              synth.activation(f"{cfg_name}.x.{n}", 1, n)) for dt, n, r in cfg]
     name = {12: "q4_k_integer", 14: "q6_k_integer"}
@@ -217,6 +216,7 @@ def cpu_baseline(cfg_name, budget_s=12.0):
 
 
 DECODE_CFG = "c4_tinyllama_decode"
+DEFAULT_CFG = "c2_q4_k_llama7b_ffn"
 PREFILL_CFG_NAME = "c5_q4_k_prefill_mistral"
 
 
@@ -295,12 +295,19 @@ def run_prefill(args, world, rank, local):
     for c in range(copies):
         step(c)
     torch.cuda.synchronize()
-    if args.check and world == 1:
+    bit_exact = None
+    if rank == 0:
+        # Bit check (rank 0 holds the first row shard of every linear): wk and wq
+        # against the oracle.
         from oracle import oracle as O
-        nm, n, r = lins[1]
-        ref = O.linear("q4_k_integer", host_x[n], host_w[nm], M, n, r, os.cpu_count())
-        got = ys[nm].cpu().numpy()
-        assert np.array_equal(got.view(np.uint32), ref.view(np.uint32)), "parity failure"
+        bit_exact = True
+        for nm, n, r in lins[:2]:
+            a, b = ranges[nm]
+            ref = O.linear("q4_k_integer", host_x[n], host_w[nm][a * vtq.row_bytes(vtq.Q4_K, n):
+                                                                b * vtq.row_bytes(vtq.Q4_K, n)],
+                           M, n, b - a, os.cpu_count())
+            got = ys[nm].cpu().numpy()
+            bit_exact &= bool(np.array_equal(got.view(np.uint32), ref.view(np.uint32)))
     steps = max(1, min(args.steps, 200))
     warm = max(3, min(args.warmup, 20))
     for i in range(warm):
@@ -384,10 +391,13 @@ def run_prefill(args, world, rank, local):
                     "h2d_bytes_per_step": sum(4 * M * n for _, n, _ in lins),
                     "d2h_bytes_per_step": sum(4 * M * (ranges[nm][1] - ranges[nm][0])
                                               for nm, n, r in lins)},
-            "gpu_launches": steps * len(lins) * 2, "clocks": clk, "cpu_baseline": cpu}),
+            "gpu_launches": steps * len(lins) * 2, "clocks": clk, "cpu_baseline": cpu,
+            "bit_exact": bit_exact}),
             flush=True)
     if world > 1:
         dist.destroy_process_group()
+    if rank == 0 and not bit_exact:
+        raise SystemExit("bench: prefill output differs from the oracle")
 
 
 def prefill_cpu_sample(reps=1):
@@ -426,37 +436,53 @@ def decode_bytes_per_token(cfg, n_pos):
 
 
 def run_decode(args, world, rank, local):
-    """TinyLlama-shaped Q4_K/Q6_K model, 16 prompt + 64 greedy
+    """The decode workload: TinyLlama-shaped Q4_K/Q6_K model, 16 prompt + 64 greedy
     tokens per step of the benchmark; replicas on N GPUs (decode does not shard)."""
+    import torch
+    import torch.distributed as dist
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    line = decode_measure(args, world, rank, local)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+    if rank == 0 and not line["bit_exact"]:
+        raise SystemExit("bench: decode tokens differ from the oracle")
+
+
+def decode_measure(args, world, rank, local, sub=False):
     import torch
     import torch.distributed as dist
     import vtq
     from vtq import gguf, receipt
-    torch.cuda.set_device(local)
-    if world > 1:
-        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    from oracle import oracle as O
     cfg = gguf.TINYLLAMA
     blob = gguf.synthetic_llama(cfg)
     prompt = gguf.prompt_tokens(16, cfg["vocab"])
     n_new = 64
     sess = vtq.DecodeSession(blob, local)
-    for _ in range(max(1, args.warmup // 10)):
+    warm = max(1, args.warmup // 10)
+    for _ in range(warm):
         toks, _ = sess.run(prompt, n_new)
-    reps = max(1, min(args.steps, 20))
+    reps = max(3, min(args.steps, 20))
     clocks = ClockSampler(local)
     if world > 1:
         dist.barrier()
     clocks.start()
-    steps_ms, call_ms = 0.0, 0.0
+    steps_ms, call_ms, per = 0.0, 0.0, []
     launches = 0
+    same = True
     for _ in range(reps):
         toks2, _ = sess.run(prompt, n_new)
         a, b = sess.timing()
         steps_ms += a
         call_ms += b
+        per.append(a)
         launches += sess.launches()
+        same &= list(toks2) == list(toks)
     clk = clocks.stop()
-    assert toks2 == toks
     if world > 1:
         t = torch.tensor([steps_ms, call_ms], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -467,43 +493,52 @@ def run_decode(args, world, rank, local):
     per_tok_bytes = decode_bytes_per_token(cfg, n_pos)
     peak, peak_kind = peaks()
     achieved = per_tok_bytes / (steps_ms / reps / n_pos / 1e3) / 1e9
+    floor_tok_s = peak * 1e9 / per_tok_bytes
     rc = receipt.decode_receipt(gguf.MODEL_ID, blob, gguf.arch_string(cfg), prompt, n_new, toks)
     cpu = None
+    threads = os.cpu_count() or 1
+    t0 = time.perf_counter()
+    ref, _ = O.decode_run(blob, prompt, n_new, threads=threads)
+    el = time.perf_counter() - t0
+    exact = bool(same and list(ref) == list(toks))
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        from oracle import oracle as O
-        threads = os.cpu_count() or 1
-        t0 = time.perf_counter()
-        ref, _ = O.decode_run(blob, prompt, n_new, threads=threads)
-        el = time.perf_counter() - t0
         cpu = {"value": round(n_pos / el, 3), "unit": "tok/s", "cores": threads, "kind": "port",
-               "sample": f"one full config-4 run ({n_pos} positions) in {el:.1f} s",
-               "tokens_match": ref == toks}
-    if rank == 0:
-        print(json.dumps({
-            "metric": METRIC, "value": round(tok_s, 2), "unit": "tok/s", "n_gpus": world,
-            "steps": reps, "warmup": max(1, args.warmup // 10),
-            "ms_per_step": round(steps_ms / reps, 4), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-            "config": {"workload": DECODE_CFG, "model": "random-init TinyLlama-1.1B shapes, "
-                       "Q4_K/Q6_K GGUF", "prompt": len(prompt), "new_tokens": n_new,
-                       "parallelism": f"replicas x{world}" if world > 1 else "1 GPU",
-                       "l2": "667 MB of weights per token > L2",
-                       "prompt_batched": len(prompt) - 1,
-                       "timing": "CUDA events around one run: the batched prompt positions "
-                                 "(all but the last) and the per-token step graphs"},
-            "ms_per_token": round(steps_ms / reps / n_pos, 4),
-            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
-                         "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": None,
-                         "peak_source": peak_kind, "bytes_per_token": per_tok_bytes,
-                         "bytes_note": "every position's weights counted; the batched prompt "
-                                       "positions share weight reads"},
-            "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": 4 * len(prompt),
-                    "d2h_bytes_per_step": 4 * n_new + 4},
-            "receipt": {"model_digest": rc["model_digest"], "model_digest_v1": rc["model_digest_v1"]},
-            "gpu_launches": launches * world, "clocks": clk, "cpu_baseline": cpu}), flush=True)
+               "sample": f"one full decode run ({n_pos} positions) in {el:.1f} s"}
     sess.close()
-    if world > 1:
-        dist.destroy_process_group()
+    return {
+        "metric": METRIC, "value": round(tok_s, 2), "unit": "tok/s", "n_gpus": world,
+        "steps": reps, "warmup": warm,
+        "ms_per_step": round(steps_ms / reps, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+        "config": {"workload": DECODE_CFG, "model": "random-init TinyLlama-1.1B shapes, "
+                   "Q4_K/Q6_K GGUF", "prompt": len(prompt), "new_tokens": n_new,
+                   "parallelism": f"replicas x{world}" if world > 1 else "1 GPU",
+                   "l2": "667 MB of weights per token > L2",
+                   "prompt_batched": len(prompt) - 1,
+                   "step_kind": sess_kind_name(sess),
+                   "timing": "CUDA events around each run: the batched prompt positions "
+                             "(all but the last) and the per-token steps"},
+        "ms_per_token": round(steps_ms / reps / n_pos, 4),
+        "bit_exact": exact,
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                     "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": None,
+                     "peak_source": peak_kind, "bytes_per_token": per_tok_bytes,
+                     "hbm_floor_tok_s": round(floor_tok_s, 1),
+                     "frac_of_floor": round(tok_s / world / floor_tok_s, 4),
+                     "bytes_note": "every position's weights counted; the batched prompt "
+                                   "positions share weight reads"},
+        "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": 4 * len(prompt),
+                "d2h_bytes_per_step": 4 * n_new + 4},
+        "receipt": {"model_digest": rc["model_digest"], "model_digest_v1": rc["model_digest_v1"]},
+        "gpu_launches": launches * world, "clocks": clk, "cpu_baseline": cpu}
+
+
+def sess_kind_name(sess):
+    try:
+        return {0: "per-op graph", 1: "fused per-op graph", 2: "persistent kernel"}.get(
+            int(sess.step_kind), "?")
+    except Exception:
+        return "?"
 
 
 def run_sharded(args, world, rank, local, ctx, stream, cfg):
@@ -714,9 +749,17 @@ def main():
     ap.add_argument("--steps", type=int, default=3000)
     ap.add_argument("--warmup", type=int, default=50)
     ap.add_argument("--impl", default="vtq", choices=["vtq", "reference"])
-    ap.add_argument("--config", default="c2_q4_k_llama7b_ffn")
+    ap.add_argument("--config", default=DEFAULT_CFG)
+    ap.add_argument("--launch", default="step", choices=["step", "single"],
+                    help="k-quant matvecs: one vtq_linear_list launch per step (default) or "
+                         "one vtq_linear launch per matvec")
+    ap.add_argument("--per-launch", type=int, default=1,
+                    help="--launch step: consecutive steps per vtq_linear_list launch")
+    ap.add_argument("--min-ms", type=float, default=250.0,
+                    help="device time of the timed region (graph replays of --steps steps)")
+    ap.add_argument("--no-sub", action="store_true",
+                    help="default config: skip the Q6_K head and decode sub-results")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--check", action="store_true", help="bit-compare outputs with the oracle")
     ap.add_argument("--sharded", action="store_true",
                     help="run the row-sharded path (fused gather) even with one rank")
     ap.add_argument("--strong", action="store_true",
@@ -761,162 +804,211 @@ def main():
                                     device_id=torch.device("cuda", local))
         run_sharded(args, world, rank, local, ctx, stream, cfg)
         return
+    line = run_matvec(args, ctx, stream, args.config)
+    if not line:
+        return
+    if args.config == DEFAULT_CFG and not args.no_sub:
+        # The rest of the metric in the same run: the Q6_K head matvec and the
+        # decode loop, each bit-checked.
+        sub = run_matvec(args, ctx, stream, "c3_q6_k_head_4096x32000", sub=True)
+        line["sub"] = {"c3_q6_k_head_4096x32000": sub}
+        ctx.close()
+        torch.cuda.synchronize()
+        line["sub"][DECODE_CFG] = decode_measure(args, 1, 0, local, sub=True)
+        ok = sub["bit_exact"] and line["sub"][DECODE_CFG]["bit_exact"]
+        line["bit_exact_all"] = bool(line["bit_exact"] and ok)
+    print(json.dumps(line), flush=True)
+    if not line.get("bit_exact_all", line["bit_exact"]):
+        raise SystemExit("bench: an output differs from the oracle")
+
+
+def run_matvec(args, ctx, stream, cfg_name, sub=False):
+    """One GPU: every matvec of the configuration per step, weights resident.
+
+    The timed work is a CUDA graph of exactly --steps steps (step i reads
+    weight copy i mod copies, so the weights read between two reads of the
+    same copy exceed L2), replayed until at least --min-ms of device time has
+    passed; `value` uses the median replay. --launch step (default for
+    Q4_K/Q6_K): each step is ONE vtq_linear_list launch over the step's
+    matvecs; --launch single: one vtq_linear launch per matvec."""
+    import torch
+    import vtq
+    from vtq import synth
+    from oracle import oracle as O
+    cfg = synth.CONFIGS[cfg_name]
+    kquant = all(dt in (vtq.Q4_K, vtq.Q6_K) for dt, n, r in cfg)
+    mode = args.launch if kquant else "single"
     step_bytes = sum(algo_bytes(dt, n, r) for dt, n, r in cfg)
     wbytes = sum(r * vtq.row_bytes(dt, n) for dt, n, r in cfg)
     copies = max(1, -(-ROTATE_MIN_BYTES // wbytes))
     if args.launches_only:
         copies = 1
-    host_w = [synth.weight(dt, f"{args.config}.w.{n}x{r}", r, n) for dt, n, r in cfg]
-    host_x = [synth.activation(f"{args.config}.x.{n}", 1, n) for dt, n, r in cfg]
+    host_w = [synth.weight(dt, f"{cfg_name}.w.{n}x{r}", r, n) for dt, n, r in cfg]
+    host_x = [synth.activation(f"{cfg_name}.x.{n}", 1, n) for dt, n, r in cfg]
     weights = [[ctx.upload(dt, host_w[i], n, r) for i, (dt, n, r) in enumerate(cfg)]
                for _ in range(copies)]
     xs = [torch.from_numpy(x).cuda() for x in host_x]
     ys = [torch.empty(r, device="cuda") for dt, n, r in cfg]
+    launches_per_step = 1 if mode == "step" else len(cfg)
 
-    # Capture one rotation (copies x matvecs) as a CUDA graph; launches per
-    # graph replay = copies * len(cfg) kernels of ours.
-    def rotation(events=None):
-        for c in range(copies):
+    per = max(1, min(args.per_launch, vtq.LIST_MAX // len(cfg))) if mode == "step" else 1
+
+    def step(c, events=None, nsteps=1):
+        """nsteps consecutive steps from weight copy c on (list mode: one launch)."""
+        if events is not None:
+            events[0].record(stream)
+        if mode == "step":
+            ctx.linear_list([(weights[(c + j) % copies][i], xs[i].data_ptr(), ys[i].data_ptr())
+                             for j in range(nsteps) for i in range(len(cfg))])
+        else:
             for i in range(len(cfg)):
-                if events is not None:
-                    events[c * len(cfg) + i][0].record(stream)
                 ctx.linear_ptr(weights[c][i], xs[i].data_ptr(), ys[i].data_ptr(), 1)
-                if events is not None:
-                    events[c * len(cfg) + i][1].record(stream)
+        if events is not None:
+            events[1].record(stream)
 
-    rotation()
+    for c in range(copies):
+        step(c)
     torch.cuda.synchronize()
     if args.launches_only:
-        for _ in range(args.warmup + args.steps - 1):
-            rotation()
+        for k in range(args.warmup + args.steps - 1):
+            step(k % copies, nsteps=per)
         torch.cuda.synchronize()
-        print(json.dumps({"launches_only": True, "config": args.config,
-                          "launches": (args.warmup + args.steps) * len(cfg)}))
-        return
-    if args.check:
-        from oracle import oracle as O
-        for i, (dt, n, r) in enumerate(cfg):
-            ref = O.linear({12: "q4_k_integer", 14: "q6_k_integer"}[dt], host_x[i], host_w[i],
-                           1, n, r, os.cpu_count()) if dt in (12, 14) else \
-                O.linear_dispatch(dt, host_x[i], host_w[i], n, r, threads=os.cpu_count())
-            got = ys[i].cpu().numpy()
-            assert np.array_equal(got.view(np.uint32), ref.view(np.uint32)), "parity failure"
+        print(json.dumps({"launches_only": True, "config": cfg_name,
+                          "launches": (args.warmup + args.steps) * launches_per_step}))
+        return None
 
+    K = args.steps
     g = torch.cuda.CUDAGraph()
+    n_launch = 0
     with torch.cuda.graph(g, stream=stream, capture_error_mode="thread_local"):
-        rotation()
-    launches_per_replay = copies * len(cfg)
-    replays = max(1, -(-args.steps // (copies)))  # each replay = `copies` steps
-    steps = replays * copies
-    warm_replays = max(1, -(-args.warmup // copies))
+        for k in range(0, K, per):
+            step(k % copies, nsteps=min(per, K - k))
+            n_launch += 1 if mode == "step" else len(cfg)
+    # Warm-up: W steps (graph replays of K steps, at least one).
+    warm_replays = max(1, -(-args.warmup // K))
     for _ in range(warm_replays):
         g.replay()
     torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    g.replay()
+    b.record(stream)
+    torch.cuda.synchronize()
+    est = max(a.elapsed_time(b), 1e-3)
+    replays = max(5, int(-(-args.min_ms // est)))
 
-    # ---- timed region (device time, events on the launching stream) ----
-    clocks = ClockSampler(local)
-    if world > 1:
-        dist.barrier()
+    # ---- timed region: device time, events on the launching stream ----
+    clocks = ClockSampler(torch.cuda.current_device())
     torch.cuda.synchronize()
     clocks.start()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(replays):
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(replays + 1)]
+    evs[0].record(stream)
+    for r_ in range(replays):
         g.replay()
-    e1.record(stream)
+        evs[r_ + 1].record(stream)
     torch.cuda.synchronize()
     clk = clocks.stop()
-    if world > 1:
-        dist.barrier()
-    ms = e0.elapsed_time(e1)
-    if world > 1:
-        t = torch.tensor([ms], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-    value = step_bytes * steps * world / (ms / 1e3) / 1e9
+    per = [evs[i].elapsed_time(evs[i + 1]) for i in range(replays)]
+    total_ms = evs[0].elapsed_time(evs[-1])
+    med = statistics.median(per)
+    value = step_bytes * K / (med / 1e3) / 1e9
 
-    # ---- per-launch durations of the dominant kernel (same stream, graph-free) ----
-    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-           for _ in range(launches_per_replay)]
+    # Bit check of the outputs the timed graph left (every weight copy holds
+    # the same bytes, so every step's y is the oracle's y).
+    threads = os.cpu_count() or 1
+    exact = True
+    for i, (dt, n, r) in enumerate(cfg):
+        ref = O.linear({12: "q4_k_integer", 14: "q6_k_integer"}[dt], host_x[i], host_w[i],
+                       1, n, r, threads) if dt in (12, 14) else \
+            O.linear_dispatch(dt, host_x[i], host_w[i], n, r, threads=threads)
+        exact &= bool(np.array_equal(ys[i].cpu().numpy().view(np.uint32), ref.view(np.uint32)))
+
+    # Eager per-launch events (no graph, no programmatic overlap), for context.
+    pair = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
     durs = []
-    for _ in range(max(3, 300 // launches_per_replay)):
-        rotation(evs)
+    for k in range(max(3, 60 // len(cfg))):
+        step(k % copies, pair)
         torch.cuda.synchronize()
-        durs += [a.elapsed_time(b) for a, b in evs]
-    per_launch_bytes = statistics.mean(
-        [algo_bytes(dt, n, r) for dt, n, r in cfg])
-    eager_ms = statistics.mean(durs)
-    # The matvec is the only kernel in the timed region and its launches run
-    # back to back: its average launch duration there is the region's device
-    # time over the launches (CUDA events on the launching stream). The eager
-    # per-launch events above (no graph, no programmatic overlap, an event pair
-    # around every launch) are reported beside it.
-    avg_ms = ms / (steps * len(cfg))
+        durs.append(pair[0].elapsed_time(pair[1]) / launches_per_step)
+    per_launch_bytes = step_bytes * K / n_launch
+    avg_ms = med / n_launch
     peak, peak_kind = peaks()
     achieved = per_launch_bytes / (avg_ms / 1e3) / 1e9
-    traffic = profile_traffic(args.config)
+    traffic = profile_traffic(cfg_name, mode)
 
     # ---- e2e through the public C ABI with host buffers ----
     px = [torch.from_numpy(x).pin_memory() for x in host_x]
     py = [torch.empty(r, dtype=torch.float32).pin_memory() for dt, n, r in cfg]
-    e2e_steps = max(20, min(2000, steps // 4))
-    for _ in range(5):
-        for i in range(len(cfg)):
-            ctx.linear_ptr(weights[0][i], px[i].data_ptr(), py[i].data_ptr(), 1, host=True)
-    if world > 1:
-        dist.barrier()
+
+    def host_step(c):
+        if mode == "step":
+            ctx.linear_list([(weights[c][i], px[i].data_ptr(), py[i].data_ptr())
+                             for i in range(len(cfg))], host=True)
+        else:
+            for i in range(len(cfg)):
+                ctx.linear_ptr(weights[c][i], px[i].data_ptr(), py[i].data_ptr(), 1, host=True)
+
+    for k in range(5):
+        host_step(k % copies)
+    e2e_steps = max(20, min(2000, int(2 * args.min_ms / max(med / K, 1e-3) / 8)))
     torch.cuda.synchronize()
     f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     f0.record(stream)
-    for s in range(e2e_steps):
-        c = s % copies
-        for i in range(len(cfg)):
-            ctx.linear_ptr(weights[c][i], px[i].data_ptr(), py[i].data_ptr(), 1, host=True)
+    for k in range(e2e_steps):
+        host_step(k % copies)
     f1.record(stream)
     torch.cuda.synchronize()
     ems = f0.elapsed_time(f1)
-    if world > 1:
-        t = torch.tensor([ems], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ems = float(t.item())
-    e2e_value = step_bytes * e2e_steps * world / (ems / 1e3) / 1e9
+    e2e_value = step_bytes * e2e_steps / (ems / 1e3) / 1e9
+    e2e_exact = all(np.array_equal(py[i].numpy().view(np.uint32), ys[i].cpu().numpy().view(np.uint32))
+                    for i in range(len(cfg)))
     h2d = sum(4 * n for dt, n, r in cfg)
-    d2h = sum(4 * r + 256 for dt, n, r in cfg)
+    d2h = (256 + sum(-(-4 * r // 256) * 256 for dt, n, r in cfg)) if mode == "step" else \
+        sum(4 * r + 256 for dt, n, r in cfg)
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_baseline(args.config)
-
-    if rank == 0:
-        line = {
-            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
-            "steps": steps, "warmup": warm_replays * copies,
-            "ms_per_step": round(ms / steps, 5), "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-            "config": {"workload": args.config,
-                       "matvecs": [f"{vtq.formats.NAMES[dt]} {n}->{r}" for dt, n, r in cfg],
-                       "batch": 1, "parallelism": f"replicas x{world}" if world > 1 else "1 GPU",
-                       "l2": f"inputs larger than L2: {copies} rotating weight copies "
-                             f"({copies * wbytes / 1e6:.0f} MB)",
-                       "timing": "CUDA graph of one rotation, replayed; CUDA events"},
-            "pct_of_peak": round(100 * value / world / peak, 1),
-            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
-                         "unit": "GB/s", "frac": round(achieved / peak, 4),
-                         "traffic": traffic, "peak_source": peak_kind,
-                         "kernel": "kq_matvec_kernel",
-                         "bytes_per_launch": per_launch_bytes,
-                         "avg_launch_us": round(avg_ms * 1e3, 3),
-                         "avg_launch_source": "timed region / launches (graph replay)",
-                         "eager_launch_us": round(eager_ms * 1e3, 3)},
-            "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h, "steps": e2e_steps},
-            "gpu_launches": steps * len(cfg),
-            "clocks": clk,
-            "cpu_baseline": cpu,
-        }
-        print(json.dumps(line), flush=True)
-    if world > 1:
-        dist.destroy_process_group()
+    if not args.no_cpu_baseline:
+        cpu = {"all_cores": cpu_baseline(cfg_name, threads, budget_s=8.0 if sub else 12.0),
+               "one_core": cpu_baseline(cfg_name, 1, budget_s=4.0 if sub else 8.0)}
+        cpu = dict(cpu["all_cores"], one_core=cpu["one_core"])
+    launch_desc = (f"one vtq_linear_list launch per {per} step(s) (persistent kernel over "
+                   f"those steps' {per * len(cfg)} matvecs)" if mode == "step"
+                   else "one vtq_linear launch per matvec")
+    return {
+        "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": 1,
+        "steps": K, "warmup": warm_replays * K, "steps_match": True,
+        "ms_per_step": round(med / K, 5), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+        "config": {"workload": cfg_name,
+                   "matvecs": [f"{vtq.formats.NAMES[dt]} {n}->{r}" for dt, n, r in cfg],
+                   "batch": 1, "parallelism": "1 GPU",
+                   "l2": f"inputs larger than L2: {copies} rotating weight copies "
+                         f"({copies * wbytes / 1e6:.0f} MB)",
+                   "launch": launch_desc,
+                   "timing": f"CUDA graph of the {K} steps, replayed {replays} times "
+                             f"({total_ms:.0f} ms of device time); value from the median "
+                             "replay; CUDA events on the launching stream"},
+        "pct_of_peak": round(100 * value / peak, 1),
+        "bit_exact": exact,
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                     "unit": "GB/s", "frac": round(achieved / peak, 4),
+                     "traffic": traffic, "peak_source": peak_kind,
+                     "kernel": "kq_list_kernel" if mode == "step" else
+                     ("kq_matvec_kernel" if kquant else "canon_matvec_kernel"),
+                     "bytes_per_launch": per_launch_bytes,
+                     "avg_launch_us": round(avg_ms * 1e3, 3),
+                     "avg_launch_source": "median graph replay / launches in it",
+                     "eager_launch_us": round(1e3 * statistics.mean(durs), 3),
+                     "replay_ms_min_med_max": [round(min(per), 4), round(med, 4),
+                                               round(max(per), 4)]},
+        "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "steps": e2e_steps, "bit_exact": e2e_exact,
+                "call": "vtq_linear_list with VTQ_PTR_HOST (pinned x in, y out)"
+                if mode == "step" else "vtq_linear with VTQ_PTR_HOST per matvec"},
+        "gpu_launches": n_launch * replays,
+        "clocks": clk,
+        "cpu_baseline": cpu,
+    }
 
 
 if __name__ == "__main__":

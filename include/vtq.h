@@ -87,6 +87,29 @@ vtq_status vtq_weight_info(const vtq_weight* w, int32_t* dtype, int64_t* in_feat
 vtq_status vtq_linear(vtq_ctx* ctx, const vtq_weight* w, const float* x, float* y, int64_t batch,
                       uint32_t flags);
 
+/* A list of integer k-quant linears (Q4_K / Q6_K weights, batch 1, device
+ * pointers) run by ONE persistent kernel launch, in list order, async on the
+ * context stream. Replaces a run of consecutive linear_dispatch calls
+ * (src/model/forward_quantized.rs:663-785, made 7 times per layer) with one
+ * launch: each item's y is bit-identical to vtq_linear on the same inputs,
+ * but the next item's weights stream from HBM while the current one is still
+ * being reduced, so no kernel boundary sits between the linears.
+ * wait_for = j (an earlier item) makes item i read x only after every row of
+ * item j's y has been stored -- use it when x is (or is computed from) y_j;
+ * -1 means x is ready when the call is made. Calls on one context share its
+ * completion counters: run them on one stream (the context's).
+ * flags VTQ_PTR_HOST: x and y are host pointers (no wait_for); the call copies
+ * every x in, runs the one launch, reads every y back with one copy and
+ * returns when they are written. */
+#define VTQ_LIST_MAX 32
+typedef struct vtq_list_item {
+  const vtq_weight* w;
+  const float* x; /* device, in_feat floats */
+  float* y;       /* device, rows floats */
+  int32_t wait_for;
+} vtq_list_item;
+vtq_status vtq_linear_list(vtq_ctx* ctx, const vtq_list_item* items, int32_t n, uint32_t flags);
+
 /* linear_dispatch with host slices (src/model/forward_quantized.rs:663-668,
  * batch 1): uploads `w` on every call. For parity tests and one-off calls;
  * resident weights go through vtq_weight_upload + vtq_linear. */

@@ -50,11 +50,51 @@ struct KqParams {
   int epi;                  // 1: rows come in (gate, up) pairs; y[b, r / 2] = silu(gate) * up
 };
 
+// quantize_block_q8 (quant.rs:750-771) of one 256-element block held by a
+// warp (8 contiguous values per lane): the block's int8 codes (8 per lane) go
+// to xqb, its scale d to *xdp (lane 0) and its activation sums -- NB = 8: one
+// per 32 elements (Q4_K's bsums), NB = 16: one per 16 (the Q6_K -32 offset
+// term) -- to bs[0..NB). Shared or global destinations.
+template <int NB>
+__device__ __forceinline__ void quant_block(const float (&v)[8], int lane, int8_t* xqb, int* bs,
+                                            float* xdp) {
+  // amax = max over non-NaN |v|, starting at +0.0 (quant.rs:752-758).
+  uint32_t am = 0;
+#pragma unroll
+  for (int i = 0; i < 8; i++) {
+    const uint32_t bits = __float_as_uint(v[i]) & 0x7fffffffu;
+    if (bits <= 0x7f800000u) am = max(am, bits);
+  }
+  am = __reduce_max_sync(FULL, am);
+  const float d = __fdiv_rn(__uint_as_float(am), 127.0f);
+  const float inv = (d != 0.0f) ? __fdiv_rn(1.0f, d) : 0.0f;
+  int sum = 0;
+  uint32_t w0 = 0, w1 = 0;
+#pragma unroll
+  for (int i = 0; i < 8; i++) {
+    const int q = q8_round(__fmul_rn(v[i], inv));
+    sum += q;
+    if (i < 4) w0 |= (uint32_t)(q & 0xff) << (8 * i);
+    else w1 |= (uint32_t)(q & 0xff) << (8 * (i - 4));
+  }
+  const int s16 = sum + __shfl_xor_sync(FULL, sum, 1);
+  const int s32 = s16 + __shfl_xor_sync(FULL, s16, 2);
+  if (NB == 8) {
+    if ((lane & 3) == 0) bs[lane >> 2] = s32;
+  } else {
+    if ((lane & 1) == 0) bs[lane >> 1] = s16;
+  }
+  *reinterpret_cast<uint2*>(xqb + lane * 8) = make_uint2(w0, w1);
+  if (lane == 0) *xdp = d;
+}
+
 // quantize_block_q8 for every (batch row, superblock): one warp per block,
 // 8 contiguous elements per lane. NB = 8 (sums per 32: Q4_K's bsums) or 16
 // (sums per 16: the Q6_K -32 offset term). `xs` is the activation source:
 // the TMA-staged rows in shared memory (row stride n) or global x (ldx).
-template <int NB, int CW>
+// CG: load x at L2 (ld.global.cg), for rows written by other CTAs of the
+// same launch (read after an acquire of their completion counter).
+template <int NB, int CW, bool CG = false>
 __device__ __forceinline__ void quantize_x(const KqParams& p, const float* xs, int64_t lds,
                                            int warp, int lane, float* xd, int* bsum, int8_t* xq,
                                            float xscale) {
@@ -64,48 +104,23 @@ __device__ __forceinline__ void quantize_x(const KqParams& p, const float* xs, i
     const float* src = xs + (int64_t)b * lds + s * 256 + lane * 8;
     float v[8];
     if ((reinterpret_cast<uintptr_t>(src) & 15u) == 0) {
-      const float4 a = *reinterpret_cast<const float4*>(src);
-      const float4 c = *(reinterpret_cast<const float4*>(src) + 1);
+      const float4 a = CG ? __ldcg(reinterpret_cast<const float4*>(src))
+                          : *reinterpret_cast<const float4*>(src);
+      const float4 c = CG ? __ldcg(reinterpret_cast<const float4*>(src) + 1)
+                          : *(reinterpret_cast<const float4*>(src) + 1);
       v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
       v[4] = c.x; v[5] = c.y; v[6] = c.z; v[7] = c.w;
     } else {
 #pragma unroll
-      for (int i = 0; i < 8; i++) v[i] = src[i];
+      for (int i = 0; i < 8; i++) v[i] = CG ? __ldcg(src + i) : src[i];
     }
     if (p.xf.kind == 2) {  // RMSNorm output (v already holds x + delta)
       const float* nw = p.xf.nw + s * 256 + lane * 8;
 #pragma unroll
       for (int i = 0; i < 8; i++) v[i] = __fmul_rn(__fmul_rn(v[i], xscale), nw[i]);
     }
-    // amax = max over non-NaN |v|, starting at +0.0 (quant.rs:752-758).
-    uint32_t am = 0;
-#pragma unroll
-    for (int i = 0; i < 8; i++) {
-      const uint32_t bits = __float_as_uint(v[i]) & 0x7fffffffu;
-      if (bits <= 0x7f800000u) am = max(am, bits);
-    }
-    am = __reduce_max_sync(FULL, am);
-    const float d = __fdiv_rn(__uint_as_float(am), 127.0f);
-    const float inv = (d != 0.0f) ? __fdiv_rn(1.0f, d) : 0.0f;
-    int sum = 0;
-    uint32_t w0 = 0, w1 = 0;
-#pragma unroll
-    for (int i = 0; i < 8; i++) {
-      const int q = q8_round(__fmul_rn(v[i], inv));
-      sum += q;
-      if (i < 4) w0 |= (uint32_t)(q & 0xff) << (8 * i);
-      else w1 |= (uint32_t)(q & 0xff) << (8 * (i - 4));
-    }
-    const int s16 = sum + __shfl_xor_sync(FULL, sum, 1);
-    const int s32 = s16 + __shfl_xor_sync(FULL, s16, 2);
     const int blk = b * p.S + s;
-    if (NB == 8) {
-      if ((lane & 3) == 0) bsum[blk * BsumStride<8>::v + (lane >> 2)] = s32;
-    } else {
-      if ((lane & 1) == 0) bsum[blk * BsumStride<16>::v + (lane >> 1)] = s16;
-    }
-    *reinterpret_cast<uint2*>(xq + blk * XQ_STRIDE + lane * 8) = make_uint2(w0, w1);
-    if (lane == 0) xd[blk] = d;
+    quant_block<NB>(v, lane, xq + blk * XQ_STRIDE, bsum + blk * BsumStride<NB>::v, xd + blk);
   }
 }
 

@@ -26,6 +26,8 @@ struct vtq_ctx {
   uint8_t* hio = nullptr;
   size_t hio_cap = 0;
   cudaEvent_t done = nullptr;  // end of a host-pointer call (polled, not blocked on)
+  unsigned* list_cnt = nullptr;  // completion counters of vtq_linear_list (zeroed, left zeroed)
+  uint8_t* list_rec = nullptr;   // vtq_linear_list's quantised activations (KQ_LIST_MAX records)
   std::string err;
 };
 
@@ -286,7 +288,13 @@ vtq_status vtq_init(int device, vtq_ctx** out) {
     return VTQ_ERR_GPU;
   }
   c->stream = c->own;
-  if (ensure_io(c, kStatusBytes + 64 * 1024) != VTQ_OK) {
+  if (ensure_io(c, kStatusBytes + 64 * 1024) != VTQ_OK ||
+      cudaMalloc(&c->list_cnt, (KQ_LIST_MAX + 2) * sizeof(unsigned)) != cudaSuccess ||
+      cudaMemset(c->list_cnt, 0, (KQ_LIST_MAX + 2) * sizeof(unsigned)) != cudaSuccess ||
+      cudaMalloc(&c->list_rec, KQ_LIST_MAX * KQ_LIST_REC) != cudaSuccess) {
+    if (c->io) cudaFree(c->io);
+    if (c->list_cnt) cudaFree(c->list_cnt);
+    if (c->list_rec) cudaFree(c->list_rec);
     cudaStreamDestroy(c->own);
     delete c;
     return VTQ_ERR_OOM;
@@ -300,6 +308,8 @@ vtq_status vtq_destroy(vtq_ctx* c) {
   cudaSetDevice(c->device);
   cudaStreamSynchronize(c->stream);
   if (c->io) cudaFree(c->io);
+  if (c->list_cnt) cudaFree(c->list_cnt);
+  if (c->list_rec) cudaFree(c->list_rec);
   if (c->hio) cudaFreeHost(c->hio);
   if (c->done) cudaEventDestroy(c->done);
   if (c->own) cudaStreamDestroy(c->own);
@@ -372,6 +382,76 @@ vtq_status vtq_linear(vtq_ctx* c, const vtq_weight* w, const float* x, float* y,
   if (vtq_status s = check_kernel_limits(c, w->m, flags)) return s;
   VTQ_CUDA(c, run_linear(w->m, x, w->m.in_feat, y, w->m.out_feat, batch, flags,
                          reinterpret_cast<unsigned*>(c->io), c->stream));
+  return VTQ_OK;
+}
+
+vtq_status vtq_linear_list(vtq_ctx* c, const vtq_list_item* items, int32_t n, uint32_t flags) {
+  if (!c || (!items && n)) return fail(c, VTQ_ERR_INVALID_ARG, "null argument");
+  if (n == 0) return VTQ_OK;
+  if (n < 0 || n > VTQ_LIST_MAX)
+    return fail(c, VTQ_ERR_INVALID_ARG, "vtq_linear_list: 1..VTQ_LIST_MAX items");
+  if (flags & VTQ_Q4K_FLOAT)
+    return fail(c, VTQ_ERR_NOT_IMPLEMENTED, "vtq_linear_list: not implemented (integer regime only)");
+  static_assert(VTQ_LIST_MAX == KQ_LIST_MAX, "list capacity");
+  const bool host = (flags & VTQ_PTR_HOST) != 0;
+  KqListItem it[KQ_LIST_MAX];
+  size_t yoff[KQ_LIST_MAX], xoff[KQ_LIST_MAX], end = kStatusBytes;
+  for (int i = 0; i < n; i++) {
+    const vtq_list_item& s = items[i];
+    if (!s.w || !s.x || !s.y) return fail(c, VTQ_ERR_INVALID_ARG, "vtq_linear_list: null item field");
+    if (s.w->m.dtype != T_Q4_K && s.w->m.dtype != T_Q6_K)
+      return fail(c, VTQ_ERR_NOT_IMPLEMENTED,
+                  "vtq_linear_list: not implemented (weight dtype not Q4_K / Q6_K)");
+    if (s.w->device != c->device)
+      return fail(c, VTQ_ERR_INVALID_ARG, "vtq_linear_list: weight on another device");
+    if (s.wait_for < -1 || s.wait_for >= i)
+      return fail(c, VTQ_ERR_INVALID_ARG, "vtq_linear_list: wait_for must name an earlier item");
+    if (host && s.wait_for >= 0)
+      return fail(c, VTQ_ERR_INVALID_ARG,
+                  "vtq_linear_list: wait_for needs device pointers (x would be a device y)");
+    if (vtq_status st = check_kernel_limits(c, s.w->m, 0)) return st;
+    it[i] = KqListItem{s.w->m, s.x, s.y, s.wait_for};
+    yoff[i] = end;
+    end = (end + (size_t)s.w->m.out_feat * 4 + 255) / 256 * 256;
+  }
+  VTQ_CUDA(c, cudaSetDevice(c->device));
+  unsigned* dstat = reinterpret_cast<unsigned*>(c->io);
+  if (!host) {
+    VTQ_CUDA(c, launch_kq_list(it, n, c->list_cnt, c->list_rec, dstat, c->stream));
+    return VTQ_OK;
+  }
+  // Host pointers: device io buffer [status | y_0 | y_1 ... | x_0 | x_1 ...];
+  // x's go in by DMA (straight from page-locked memory, else staged), one
+  // D2H copy brings back the status word and every y.
+  const size_t ybytes_end = end;
+  for (int i = 0; i < n; i++) {
+    xoff[i] = end;
+    end = (end + (size_t)items[i].w->m.in_feat * 4 + 255) / 256 * 256;
+  }
+  if (vtq_status s = ensure_io(c, end)) return s;
+  if (vtq_status s = ensure_hio(c, end)) return s;
+  for (int i = 0; i < n; i++) {
+    const size_t xb = (size_t)items[i].w->m.in_feat * 4;
+    const void* src = items[i].x;
+    if (!host_pinned(src)) {
+      memcpy(c->hio + xoff[i], src, xb);
+      src = c->hio + xoff[i];
+    }
+    VTQ_CUDA(c, cudaMemcpyAsync(c->io + xoff[i], src, xb, cudaMemcpyHostToDevice, c->stream));
+    it[i].x = reinterpret_cast<const float*>(c->io + xoff[i]);
+    it[i].y = reinterpret_cast<float*>(c->io + yoff[i]);
+  }
+  VTQ_CUDA(c, launch_kq_list(it, n, c->list_cnt, c->list_rec, dstat, c->stream));
+  VTQ_CUDA(c, cudaMemcpyAsync(c->hio, c->io, ybytes_end, cudaMemcpyDeviceToHost, c->stream));
+  if (vtq_status s = wait_call(c)) return s;
+  for (int i = 0; i < n; i++)
+    memcpy(items[i].y, c->hio + yoff[i], (size_t)items[i].w->m.out_feat * 4);
+  uint32_t st0;
+  memcpy(&st0, c->hio, 4);
+  if (st0 != 0) {
+    VTQ_CUDA(c, cudaMemsetAsync(c->io, 0, 4, c->stream));
+    return fail(c, VTQ_ERR_TIMEOUT, "vtq_linear_list: a device-side wait timed out");
+  }
   return VTQ_OK;
 }
 

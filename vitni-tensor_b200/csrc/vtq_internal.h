@@ -78,6 +78,25 @@ cudaError_t launch_kq_matvec(const DevMatrix& m, const float* x, int64_t ldx, in
                              float* y, int64_t ldy, unsigned* status, cudaStream_t st,
                              const GatherTarget* g = nullptr, const KqXform* xf = nullptr);
 
+// One persistent launch over a list of integer k-quant linears (batch 1), in
+// list order; item i's y is bit-identical to launch_kq_matvec on the same
+// inputs. wait_for = j (< i) makes item i read its x only after every row of
+// item j's y is stored (x may be y_j); -1 = x is ready at launch. `counters`
+// is a zeroed device array of KQ_LIST_MAX + 2 words owned by the caller; the
+// kernel leaves it zeroed. `xrec` is caller-owned scratch of KQ_LIST_MAX *
+// KQ_LIST_REC bytes (the quantised activations). Launches sharing counters
+// or scratch must be ordered on one stream.
+constexpr int KQ_LIST_MAX = 32;
+constexpr size_t KQ_LIST_REC = 45568;  // 128 superblocks: xd 512 + bsum 128*80 + xq 128*272
+struct KqListItem {
+  DevMatrix m;
+  const float* x;
+  float* y;
+  int wait_for;
+};
+cudaError_t launch_kq_list(const KqListItem* items, int n, unsigned* counters, uint8_t* xrec,
+                           unsigned* status, cudaStream_t st);
+
 // Waits on `st` until this rank's arrival counter has received `signals` more
 // arrivals than before (`expected` is a device counter of arrivals consumed).
 // Bounded: after 2 s the status word gets KERR_TIMEOUT.

@@ -20,7 +20,7 @@ import numpy as np
 from .formats import (F32, Q4_0, Q5_0, Q8_0, Q4_K, Q6_K, QuantTensor, row_bytes)  # noqa: F401
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_HERE, "libvtq.so")
+LIB_PATH = os.environ.get("VTQ_LIBRARY") or os.path.join(_HERE, "libvtq.so")
 
 PTR_HOST = 1
 Q4K_FLOAT = 2
@@ -41,7 +41,7 @@ EXPORTS = (
     "vtq_gather_create", "vtq_gather_connect", "vtq_gather_y", "vtq_linear_gather",
     "vtq_gather_wait", "vtq_gather_destroy", "vtq_libm_sweep_device", "vtq_linear_gather_wait",
     "vtq_decode_timing", "vtq_decode_debug_buffer", "vtq_decode_step_kind",
-    "vtq_exact_sum_host", "vtq_exact_sum_device", "vtq_decode_launches",
+    "vtq_exact_sum_host", "vtq_exact_sum_device", "vtq_decode_launches", "vtq_linear_list",
 )
 
 
@@ -87,6 +87,15 @@ _ERRORS = {c.status: c for c in (Internal, NotImplementedOp, GpuError, OutOfMemo
                                  InvalidArg, Malformed, Truncated)}
 
 _lib = None
+
+
+class ListItem(ctypes.Structure):
+    """vtq_list_item (include/vtq.h)."""
+    _fields_ = [("w", ctypes.c_void_p), ("x", ctypes.c_void_p), ("y", ctypes.c_void_p),
+                ("wait_for", ctypes.c_int32)]
+
+
+LIST_MAX = 32
 
 
 def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
@@ -144,6 +153,7 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         "vtq_gather_wait": (c_i32, [c_p, c_p, c_u32]),
         "vtq_gather_destroy": (c_i32, [c_p]),
         "vtq_libm_sweep_device": (c_i32, [c_p, c_sz, c_p]),
+        "vtq_linear_list": (c_i32, [c_p, c_p, c_i32, c_u32]),
         "vtq_linear_gather_wait": (c_i32, [c_p, c_p, c_p, c_i64, c_p, c_i64, c_i64, c_i64, c_u32,
                                            c_u32]),
     }
@@ -246,6 +256,16 @@ class Context:
         """vtq_linear on raw pointers (device pointers unless host=True)."""
         flags = (PTR_HOST if host else 0) | (Q4K_FLOAT if q4k_float else 0)
         self._check(self.lib.vtq_linear(self.handle, w.handle, x_ptr, y_ptr, batch, flags))
+
+    def linear_list(self, items, host: bool = False):
+        """vtq_linear_list: items are (Weight, x_ptr, y_ptr[, wait_for]), device
+        pointers (host pointers with host=True), run as one persistent launch in
+        list order."""
+        arr = (ListItem * len(items))()
+        for i, it in enumerate(items):
+            w, xp, yp = it[:3]
+            arr[i] = ListItem(w.handle, xp, yp, it[3] if len(it) > 3 else -1)
+        self._check(self.lib.vtq_linear_list(self.handle, arr, len(items), PTR_HOST if host else 0))
 
 
 # -- reference-signature functions (host slices) ---------------------------------
