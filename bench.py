@@ -753,8 +753,9 @@ def main():
     ap.add_argument("--launch", default="step", choices=["step", "single"],
                     help="k-quant matvecs: one vtq_linear_list launch per step (default) or "
                          "one vtq_linear launch per matvec")
-    ap.add_argument("--per-launch", type=int, default=1,
-                    help="--launch step: consecutive steps per vtq_linear_list launch")
+    ap.add_argument("--per-launch", type=int, default=0,
+                    help="--launch step: consecutive steps per vtq_linear_list launch "
+                         "(0: one rotation of the weight copies)")
     ap.add_argument("--min-ms", type=float, default=250.0,
                     help="device time of the timed region (graph replays of --steps steps)")
     ap.add_argument("--no-sub", action="store_true",
@@ -851,7 +852,8 @@ def run_matvec(args, ctx, stream, cfg_name, sub=False):
     ys = [torch.empty(r, device="cuda") for dt, n, r in cfg]
     launches_per_step = 1 if mode == "step" else len(cfg)
 
-    per = max(1, min(args.per_launch, vtq.LIST_MAX // len(cfg))) if mode == "step" else 1
+    per_req = args.per_launch if args.per_launch > 0 else copies
+    per = max(1, min(per_req, vtq.LIST_MAX // len(cfg))) if mode == "step" else 1
 
     def step(c, events=None, nsteps=1):
         """nsteps consecutive steps from weight copy c on (list mode: one launch)."""
@@ -940,10 +942,13 @@ def run_matvec(args, ctx, stream, cfg_name, sub=False):
     px = [torch.from_numpy(x).pin_memory() for x in host_x]
     py = [torch.empty(r, dtype=torch.float32).pin_memory() for dt, n, r in cfg]
 
+    host_calls = [ctx.prepare_list([(weights[c][i], px[i].data_ptr(), py[i].data_ptr())
+                                    for i in range(len(cfg))], host=True)
+                  for c in range(copies)] if mode == "step" else None
+
     def host_step(c):
         if mode == "step":
-            ctx.linear_list([(weights[c][i], px[i].data_ptr(), py[i].data_ptr())
-                             for i in range(len(cfg))], host=True)
+            host_calls[c]()
         else:
             for i in range(len(cfg)):
                 ctx.linear_ptr(weights[c][i], px[i].data_ptr(), py[i].data_ptr(), 1, host=True)

@@ -118,3 +118,29 @@ def test_list_validation(ctx):
         ctx.linear_list([(w4, 16, 16, 0)])  # wait_for must name an earlier item
     with pytest.raises(vtq.InvalidArg):
         ctx.linear_list([(w4, 16, 16)] * (vtq.LIST_MAX + 1))
+
+
+@pytest.mark.parametrize("pinned", [True, False])
+def test_host_pointer_list(ctx, pinned):
+    """VTQ_PTR_HOST: page-locked x / y are read and written in place by the
+    kernel; pageable ones are staged. Both must equal the device-pointer run."""
+    import torch
+    shapes = [(vtq.Q4_K, 4096, 1100), (vtq.Q6_K, 2048, 300), (vtq.Q4_K, 11008, 77)]
+    ws, xs, ys, host = _setup(ctx, shapes, "host")
+    ctx.linear_list([(w, x.data_ptr(), y.data_ptr()) for w, x, y in zip(ws, xs, ys)])
+    torch.cuda.synchronize()
+    want = [y.cpu().numpy() for y in ys]
+    for rep in range(2):
+        if pinned:
+            hx = [torch.from_numpy(x).pin_memory() for _, x in host]
+            hy = [torch.full((r,), float("nan")).pin_memory() for _, _, r in shapes]
+            ptrs = [(t.data_ptr(), u.data_ptr()) for t, u in zip(hx, hy)]
+            out = lambda: [u.numpy() for u in hy]
+        else:
+            hx = [np.array(x) for _, x in host]
+            hy = [np.full(r, np.nan, np.float32) for _, _, r in shapes]
+            ptrs = [(t.ctypes.data, u.ctypes.data) for t, u in zip(hx, hy)]
+            out = lambda: hy
+        ctx.linear_list([(w, px, py) for w, (px, py) in zip(ws, ptrs)], host=True)
+        for got, ref in zip(out(), want):
+            assert bits_equal(got, ref), rep

@@ -72,6 +72,7 @@ struct KqListParams {
   unsigned* cnt;  // [KQ_LIST_MAX] completion counters, the exit counter, the x-ready counter
   unsigned* status;
   uint8_t* xrec;  // KQ_LIST_MAX records of KQ_LIST_REC bytes
+  unsigned* hstatus;  // optional host-mapped word: the last CTA copies *status there
   int nq;         // blocks to pre-quantise (sum of S over independent items)
 };
 
@@ -365,6 +366,9 @@ __global__ void __launch_bounds__((CWL + 1) * 32, 1) kq_list_kernel(const __grid
       for (int i = 0; i < P.n; i++) P.cnt[i] = 0;
       P.cnt[KQ_LIST_MAX] = 0;
       P.cnt[KQ_LIST_MAX + 1] = 0;
+      // Completion word for a host that reads y in place: it holds a sentinel
+      // until this store, so a launch that never got here reads as failed.
+      if (P.hstatus) *reinterpret_cast<volatile unsigned*>(P.hstatus) = P.status ? *P.status : 0u;
     }
   }
 }
@@ -374,10 +378,11 @@ static inline uint32_t align_up(uint32_t v, uint32_t a) { return (v + a - 1) / a
 }  // namespace
 
 cudaError_t launch_kq_list(const KqListItem* items, int n, unsigned* counters, uint8_t* xrec,
-                           unsigned* status, cudaStream_t st) {
+                           unsigned* status, cudaStream_t st, unsigned* hstatus) {
   if (n < 1 || n > KQ_LIST_MAX || !counters || !xrec) return cudaErrorInvalidValue;
   KqListParams P{};
   P.n = n;
+  P.hstatus = hstatus;
   P.cnt = counters;
   P.xrec = xrec;
   P.status = status;

@@ -28,6 +28,7 @@ struct vtq_ctx {
   cudaEvent_t done = nullptr;  // end of a host-pointer call (polled, not blocked on)
   unsigned* list_cnt = nullptr;  // completion counters of vtq_linear_list (zeroed, left zeroed)
   uint8_t* list_rec = nullptr;   // vtq_linear_list's quantised activations (KQ_LIST_MAX records)
+  unsigned* hstat = nullptr;     // page-locked completion word of in-place host-pointer lists
   std::string err;
 };
 
@@ -122,6 +123,17 @@ bool host_pinned(const void* p) {
     return false;
   }
   return a.type == cudaMemoryTypeHost;
+}
+
+// The device address of page-locked host memory (nullptr if p is not
+// page-locked and mapped).
+void* host_mapped(const void* p) {
+  cudaPointerAttributes a{};
+  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  return a.type == cudaMemoryTypeHost ? a.devicePointer : nullptr;
 }
 
 vtq_status ensure_hio(vtq_ctx* c, size_t need) {
@@ -310,6 +322,7 @@ vtq_status vtq_destroy(vtq_ctx* c) {
   if (c->io) cudaFree(c->io);
   if (c->list_cnt) cudaFree(c->list_cnt);
   if (c->list_rec) cudaFree(c->list_rec);
+  if (c->hstat) cudaFreeHost(c->hstat);
   if (c->hio) cudaFreeHost(c->hio);
   if (c->done) cudaEventDestroy(c->done);
   if (c->own) cudaStreamDestroy(c->own);
@@ -420,7 +433,36 @@ vtq_status vtq_linear_list(vtq_ctx* c, const vtq_list_item* items, int32_t n, ui
     VTQ_CUDA(c, launch_kq_list(it, n, c->list_cnt, c->list_rec, dstat, c->stream));
     return VTQ_OK;
   }
-  // Host pointers: device io buffer [status | y_0 | y_1 ... | x_0 | x_1 ...];
+  // Host pointers, all page-locked: the kernel reads every x in place (once,
+  // in its quantisation pass) and stores every y in place; the call is one
+  // launch and a completion poll. The launch's last CTA writes the status
+  // word to page-locked memory last; a sentinel there means it never ran.
+  bool mapped = true;
+  for (int i = 0; i < n && mapped; i++) {
+    void* dx = host_mapped(items[i].x);
+    void* dy = host_mapped(items[i].y);
+    mapped = dx && dy;
+    it[i].x = static_cast<const float*>(dx);
+    it[i].y = static_cast<float*>(dy);
+  }
+  if (mapped) {
+    if (!c->hstat) VTQ_CUDA(c, cudaHostAlloc(&c->hstat, 256, cudaHostAllocMapped));
+    void* dh = host_mapped(c->hstat);
+    if (!dh) return fail(c, VTQ_ERR_GPU, "vtq_linear_list: status word not mapped");
+    *reinterpret_cast<volatile unsigned*>(c->hstat) = 0xFFFFFFFFu;
+    VTQ_CUDA(c, launch_kq_list(it, n, c->list_cnt, c->list_rec, dstat, c->stream,
+                               static_cast<unsigned*>(dh)));
+    if (vtq_status s = wait_call(c)) return s;
+    const unsigned st0 = *reinterpret_cast<volatile unsigned*>(c->hstat);
+    if (st0 != 0) {
+      VTQ_CUDA(c, cudaMemsetAsync(c->io, 0, 4, c->stream));
+      return fail(c, VTQ_ERR_TIMEOUT, st0 == 0xFFFFFFFFu
+                                          ? "vtq_linear_list: the launch did not complete"
+                                          : "vtq_linear_list: a device-side wait timed out");
+    }
+    return VTQ_OK;
+  }
+  // Otherwise: device io buffer [status | y_0 | y_1 ... | x_0 | x_1 ...];
   // x's go in by DMA (straight from page-locked memory, else staged), one
   // D2H copy brings back the status word and every y.
   const size_t ybytes_end = end;

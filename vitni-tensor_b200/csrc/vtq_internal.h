@@ -94,8 +94,10 @@ struct KqListItem {
   float* y;
   int wait_for;
 };
+// `hstatus` (optional, host-mapped): receives the status word once the whole
+// launch has finished (for callers that read y straight from host memory).
 cudaError_t launch_kq_list(const KqListItem* items, int n, unsigned* counters, uint8_t* xrec,
-                           unsigned* status, cudaStream_t st);
+                           unsigned* status, cudaStream_t st, unsigned* hstatus = nullptr);
 
 // Waits on `st` until this rank's arrival counter has received `signals` more
 // arrivals than before (`expected` is a device counter of arrivals consumed).

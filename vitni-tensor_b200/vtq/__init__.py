@@ -257,6 +257,24 @@ class Context:
         flags = (PTR_HOST if host else 0) | (Q4K_FLOAT if q4k_float else 0)
         self._check(self.lib.vtq_linear(self.handle, w.handle, x_ptr, y_ptr, batch, flags))
 
+    def prepare_list(self, items, host: bool = False):
+        """A reusable vtq_linear_list call: the item array is built once and the
+        returned function makes the C call (for repeated calls on the same
+        buffers, e.g. one decode step per call)."""
+        arr = (ListItem * len(items))()
+        for i, it in enumerate(items):
+            w, xp, yp = it[:3]
+            arr[i] = ListItem(w.handle, xp, yp, it[3] if len(it) > 3 else -1)
+        fn, h, n, fl = self.lib.vtq_linear_list, self.handle, len(items), PTR_HOST if host else 0
+        keep = [it[0] for it in items]  # the weights must outlive the call
+
+        def call():
+            st = fn(h, arr, n, fl)
+            if st:
+                self._check(st)
+        call.keep = keep
+        return call
+
     def linear_list(self, items, host: bool = False):
         """vtq_linear_list: items are (Weight, x_ptr, y_ptr[, wait_for]), device
         pointers (host pointers with host=True), run as one persistent launch in
