@@ -549,7 +549,14 @@ def run_sharded(args, world, rank, local, ctx, stream, cfg):
     matrix -- of a matrix N times taller (rank 0's shard is the N = 1 matrix,
     rank r's is drawn with its own seed), so per-GPU work stays fixed as N
     grows and the all-gather moves N times the rows. --strong: the configured
-    matrix itself is split into N contiguous row ranges (fixed total work)."""
+    matrix itself is split into N contiguous row ranges (fixed total work).
+
+    Q4_K / Q6_K with --launch step (default): one vtq_linear_list_gather launch
+    per rotation of the weight copies (the same launches as N = 1), each
+    storing its rows into every rank's y over NVLink and signalling every rank
+    once; a launch waits for the previous launch's arrivals, so ranks run at
+    most one launch apart, and the timed region ends with a wait for the last
+    launch's rows. Other formats: local matvec + NCCL all-gather per matvec."""
     import torch
     import torch.distributed as dist
     import vtq
@@ -580,100 +587,151 @@ def run_sharded(args, world, rank, local, ctx, stream, cfg):
     ys = [torch.empty(b - a, device="cuda") for a, b in rng]
     fused = all(dt in (vtq.Q4_K, vtq.Q6_K) for dt, n, r in cfg) and world <= 8 and \
         os.environ.get("VTQ_GATHER", "fused") == "fused"
+    use_list = fused and args.launch == "step"
+    per = max(1, min(copies, vtq.LIST_MAX // len(cfg))) if use_list else 1
+    steps = max(copies, min(args.steps, 2000)) // copies * copies
     offs = [sum(rows_log[:i]) for i in range(len(cfg))]
     if fused:
-        # Fused path: each matvec stores its rows into every rank's full y over
-        # NVLink; one bounded wait per step for world x len(cfg) arrivals.
         gat = vtq.Gather(ctx, sum(rows_log))
         full = [device_view(gat.y_ptr + 4 * offs[i], rows_log[i]) for i in range(len(cfg))]
     else:
         full = [torch.empty(rl, device="cuda") for rl in rows_log]
 
-    def step(c):
-        for i in range(len(cfg)):
-            if fused:
-                # The step's last matvec ends with the wait for every rank's rows.
-                last = i == len(cfg) - 1
-                gat.linear(weights[c][i], xs[i].data_ptr(), rng[i][0], rows_log[i], offs[i],
-                           wait_signals=world * len(cfg) if last else 0)
-            else:
-                ctx.linear_ptr(weights[c][i], xs[i].data_ptr(), ys[i].data_ptr(), 1)
-                dist.all_gather_into_tensor(full[i], ys[i])
+    def launch(c, nsteps, wait=True):
+        """nsteps steps from weight copy c. Fused: returns after enqueueing
+        launches that signal every rank once per launch (list) or once per
+        step (per-matvec kernels: only the step's last matvec signals, its
+        system fence covering the step's earlier stores). wait=True: the
+        launch waits for the PREVIOUS launch's arrivals from every rank;
+        wait=False starts such a chain."""
+        if use_list:
+            gat.linear_list([(weights[(c + j) % copies][i], xs[i].data_ptr(),
+                              offs[i] + rng[i][0]) for j in range(nsteps) for i in range(len(cfg))],
+                            wait_signals=world if wait else 0)
+            return
+        for j in range(nsteps):
+            for i in range(len(cfg)):
+                w = weights[(c + j) % copies][i]
+                if fused:
+                    last = i == len(cfg) - 1
+                    gat.linear(w, xs[i].data_ptr(), rng[i][0], rows_log[i], offs[i],
+                               wait_signals=world if (last and (wait or j > 0)) else 0,
+                               defer=not last)
+                else:
+                    ctx.linear_ptr(w, xs[i].data_ptr(), ys[i].data_ptr(), 1)
+                    dist.all_gather_into_tensor(full[i], ys[i])
 
-    for c in range(copies):
-        step(c)
+    def drain():
+        """Consume the one outstanding launch's arrivals (y complete everywhere)."""
+        if fused:
+            gat.wait(world)
+
+    launch(0, copies if use_list else 1, wait=False)
+    if not use_list:
+        for c in range(1, copies):
+            launch(c, 1)
+    drain()
     torch.cuda.synchronize()
     # Parity. Strong: the gathered y equals the oracle's full y bit for bit on
     # every rank. Weak: this rank's rows of the gathered y equal the oracle for
     # its shard, and every rank holds the same gathered y (bit checksum).
     from oracle import oracle as O
     threads = max(1, (os.cpu_count() or 1) // world)
+    exact = True
+    refs = []
     for i, (dt, n, r) in enumerate(cfg):
         name = {12: "q4_k_integer", 14: "q6_k_integer"}.get(dt)
         ref = O.linear(name, host_x[i], host_w[i], 1, n, r, threads) if name else \
             O.linear_dispatch(dt, host_x[i], host_w[i], n, r, threads=threads)
-        got = full[i].cpu().numpy()
-        mine = got if strong else got[rng[i][0]:rng[i][1]]
-        if not np.array_equal(mine.view(np.uint32), ref.view(np.uint32)):
-            raise SystemExit(f"rank {rank}: sharded result differs from the oracle ({args.config})")
-        bits = torch.tensor([int(got.view(np.uint32).astype(np.uint64).sum() % (1 << 62))],
-                            dtype=torch.int64, device="cuda")
-        hi, lo = bits.clone(), bits.clone()
-        dist.all_reduce(hi, op=dist.ReduceOp.MAX)
-        dist.all_reduce(lo, op=dist.ReduceOp.MIN)
-        if int(hi.item()) != int(lo.item()):
-            raise SystemExit(f"rank {rank}: ranks hold different gathered y ({args.config})")
-    steps = max(copies, min(args.steps, 2000)) // copies * copies
-    for i in range(max(3, args.warmup)):
-        step(i % copies)
+        refs.append(ref)
+
+    def check():
+        ok = True
+        for i, (dt, n, r) in enumerate(cfg):
+            got = full[i].cpu().numpy()
+            mine = got if strong else got[rng[i][0]:rng[i][1]]
+            ok &= bool(np.array_equal(mine.view(np.uint32), refs[i].view(np.uint32)))
+            bits = torch.tensor([int(got.view(np.uint32).astype(np.uint64).sum() % (1 << 62))],
+                                dtype=torch.int64, device="cuda")
+            hi, lo = bits.clone(), bits.clone()
+            dist.all_reduce(hi, op=dist.ReduceOp.MAX)
+            dist.all_reduce(lo, op=dist.ReduceOp.MIN)
+            ok &= int(hi.item()) == int(lo.item())
+        return ok
+
+    exact &= check()
+    K = args.steps if fused else steps
+
+    def block():
+        """K steps that start and end with no arrival outstanding."""
+        for k in range(0, K, per):
+            launch(k % copies, min(per, K - k), wait=k > 0)
+        drain()
+
+    for _ in range(max(1, -(-max(3, args.warmup) // K))):
+        block()
     torch.cuda.synchronize()
     graph = None
     if fused:
-        # One rotation (copies steps) as a CUDA graph, replayed.
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph, stream=stream, capture_error_mode="thread_local"):
-            for c in range(copies):
-                step(c)
+            block()
         graph.replay()
         torch.cuda.synchronize()
+    run_block = graph.replay if graph is not None else block
+    a_, b_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a_.record(stream)
+    run_block()
+    b_.record(stream)
+    torch.cuda.synchronize()
+    est = torch.tensor([max(a_.elapsed_time(b_), 1e-3)], device="cuda")
+    dist.all_reduce(est, op=dist.ReduceOp.MAX)
+    replays = max(5, int(-(-args.min_ms // float(est.item()))))
     clocks = ClockSampler(local)
     dist.barrier()
     torch.cuda.synchronize()
     clocks.start()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    if graph is not None:
-        for _ in range(steps // copies):
-            graph.replay()
-    else:
-        for i in range(steps):
-            step(i % copies)
-    e1.record(stream)
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(replays + 1)]
+    evs[0].record(stream)
+    for r_ in range(replays):
+        run_block()
+        evs[r_ + 1].record(stream)
     torch.cuda.synchronize()
     clk = clocks.stop()
     dist.barrier()
-    ms = torch.tensor([e0.elapsed_time(e1)], device="cuda")
+    exact &= check()  # the timed launches' gathered y
+    rep_ms = [evs[i].elapsed_time(evs[i + 1]) for i in range(replays)]
+    ms = torch.tensor([statistics.median(rep_ms)], device="cuda")
     dist.all_reduce(ms, op=dist.ReduceOp.MAX)
     ms = float(ms.item())
+    steps = K
     step_bytes = sum(algo_bytes(dt, n, r) for dt, n, r in cfg) * (1 if strong else world)
     value = step_bytes * steps / (ms / 1e3) / 1e9
     # Local kernel time alone (no collective), for the roofline of the shard.
-    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-           for _ in cfg]
+    ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
     durs = []
-    for k in range(50):
-        for i in range(len(cfg)):
-            evs[i][0].record(stream)
-            ctx.linear_ptr(weights[k % copies][i], xs[i].data_ptr(), ys[i].data_ptr(), 1)
-            evs[i][1].record(stream)
+    for k in range(20):
+        ev[0].record(stream)
+        if use_list:
+            ctx.linear_list([(weights[(k + j) % copies][i], xs[i].data_ptr(), ys[i].data_ptr())
+                             for j in range(per) for i in range(len(cfg))])
+        else:
+            for i in range(len(cfg)):
+                ctx.linear_ptr(weights[k % copies][i], xs[i].data_ptr(), ys[i].data_ptr(), 1)
+        ev[1].record(stream)
         torch.cuda.synchronize()
-        durs += [a.elapsed_time(b) for a, b in evs]
-    local_bytes = statistics.mean(
+        durs.append(ev[0].elapsed_time(ev[1]))
+    launch_steps = per if use_list else 1
+    local_bytes = launch_steps * sum(
         (b - a) * vtq.row_bytes(dt, n) + 4 * n + 4 * (b - a) for (dt, n, r), (a, b) in zip(cfg, rng))
+    if not use_list:
+        local_bytes /= len(cfg)
     peak, peak_kind = peaks()
-    achieved = local_bytes / (statistics.mean(durs) / 1e3) / 1e9
+    avg_launch = statistics.median(durs) / (1 if use_list else len(cfg))
+    achieved = local_bytes / (avg_launch / 1e3) / 1e9
     gather_bytes = sum(4 * rl for rl in rows_log)
-    # e2e: pinned host x -> device, local matvec, all-gather, full y -> pinned host.
+    # e2e: pinned host x -> device, local matvecs + gather, full y -> pinned host,
+    # lock-step (each step waits for its own arrivals before y is copied out).
     px = [torch.from_numpy(x).pin_memory() for x in host_x]
     py = [torch.empty(rl, dtype=torch.float32).pin_memory() for rl in rows_log]
     e2e_steps = max(20, min(1000, steps // 2))
@@ -684,12 +742,11 @@ def run_sharded(args, world, rank, local, ctx, stream, cfg):
     for k in range(e2e_steps):
         for i in range(len(cfg)):
             xs[i].copy_(px[i], non_blocking=True)
-            if fused:
-                gat.linear(weights[k % copies][i], xs[i].data_ptr(), rng[i][0], rows_log[i],
-                           offs[i], wait_signals=world * len(cfg) if i == len(cfg) - 1 else 0)
-            else:
-                ctx.linear_ptr(weights[k % copies][i], xs[i].data_ptr(), ys[i].data_ptr(), 1)
-                dist.all_gather_into_tensor(full[i], ys[i])
+        if fused:
+            launch(k % copies, 1, wait=False)
+            drain()
+        else:
+            launch(k % copies, 1)
         for i in range(len(cfg)):
             py[i].copy_(full[i], non_blocking=True)
     f1.record(stream)
@@ -699,10 +756,14 @@ def run_sharded(args, world, rank, local, ctx, stream, cfg):
     e2e = {"value": round(step_bytes * e2e_steps / (float(ems.item()) / 1e3) / 1e9, 2),
            "unit": "GB/s", "h2d_bytes_per_step": sum(4 * n for dt, n, r in cfg),
            "d2h_bytes_per_step": sum(4 * rl for rl in rows_log), "steps": e2e_steps}
+    flag = torch.tensor([1 if exact else 0], device="cuda")
+    dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+    exact = bool(flag.item())
     if rank == 0:
         print(json.dumps({
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
             "steps": steps, "warmup": max(3, args.warmup), "ms_per_step": round(ms / steps, 5),
+            "steps_match": steps == args.steps,
             "higher_is_better": True, "scaling": "strong" if strong else "weak",
             "vs_baseline": None, "dtype": "int8", "data": "synthetic",
             "config": {"workload": args.config,
@@ -710,27 +771,41 @@ def run_sharded(args, world, rank, local, ctx, stream, cfg):
                        "batch": 1,
                        "shards": ("the configured matrices split over the ranks" if strong else
                                   "each rank: a full-size shard of an N-times taller matrix"),
-                       "parallelism": f"rows sharded x{world} + " + ("fused NVLink all-gather (each matvec stores its rows into every rank's y)" if fused else "NCCL all-gather of y"),
+                       "parallelism": f"rows sharded x{world} + " + (
+                           f"fused NVLink all-gather in one vtq_linear_list_gather launch per "
+                           f"{per} steps (rows stored into every rank's y, one arrival signal "
+                           "per launch, waited for one launch later)" if use_list else
+                           "fused NVLink all-gather per matvec" if fused else
+                           "NCCL all-gather of y"),
                        "l2": f"inputs larger than L2: {copies} rotating weight copies per rank "
                              f"({copies * wbytes / 1e6:.0f} MB)",
-                       "timing": ("CUDA graph of one rotation (fused matvec+gather kernels and the "
-                                  "arrival wait), replayed" if fused else
-                                  "eager launches (kernel + all_gather per matvec)") +
+                       "timing": (f"CUDA graph of the {steps} steps ending with the wait for the "
+                                  f"last launch's rows, replayed {replays} times; median replay"
+                                  if fused else
+                                  f"{replays} eager blocks of {steps} steps (kernel + all_gather "
+                                  "per matvec); median block") +
                                  "; CUDA events, max over ranks"},
+            "bit_exact": exact,
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
                          "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": None,
-                         "peak_source": peak_kind, "kernel": "kq_matvec_kernel (local shard)",
+                         "peak_source": peak_kind,
+                         "kernel": "kq_list_kernel (local shard)" if use_list else
+                         "kq_matvec_kernel (local shard)",
                          "bytes_per_launch": local_bytes,
-                         "avg_launch_us": round(1e3 * statistics.mean(durs), 3)},
+                         "avg_launch_us": round(1e3 * avg_launch, 3)},
             "nvlink": {"all_gather_bytes_per_step": gather_bytes},
-            "parity": "gathered y bit-identical to the oracle on every rank",
-            "e2e": e2e, "gpu_launches": steps * len(cfg), "clocks": clk,
-            "cpu_baseline": None}), flush=True)
+            "parity": "gathered y bit-identical to the oracle on every rank, before and after "
+                      "the timed region",
+            "e2e": e2e, "gpu_launches": replays * ((-(-steps // per) + 1) if use_list
+                                                   else steps * len(cfg) + 1),
+            "clocks": clk, "cpu_baseline": None}), flush=True)
     if fused:
         torch.cuda.synchronize()
         dist.barrier()
         gat.close()
     dist.destroy_process_group()
+    if not exact:
+        raise SystemExit(f"rank {rank}: sharded result differs from the oracle")
 
 
 def device_view(ptr, n):

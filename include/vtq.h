@@ -44,6 +44,8 @@ typedef int32_t vtq_status;
 #define VTQ_PTR_HOST 1u  /* x and y are host pointers; the call copies x in and y out and returns
                             when y is written. Otherwise x/y are device pointers and the call is
                             asynchronous on the context stream. */
+#define VTQ_GATHER_DEFER 4u /* vtq_linear_gather: do not signal arrival; a later gathered launch on
+                              the same stream signals for this one too */
 #define VTQ_Q4K_FLOAT 2u /* Q4_K in the reference's default-feature regime (float-fused canonical,
                             quant.rs:616-702) instead of the `std-parallel` integer regime. */
 
@@ -58,7 +60,14 @@ vtq_status vtq_destroy(vtq_ctx* ctx);
 const char* vtq_last_error(const vtq_ctx* ctx);
 /* Use the caller's cudaStream_t (NULL = the context's own stream). */
 vtq_status vtq_set_stream(vtq_ctx* ctx, void* cuda_stream);
+/* Wait for the context stream; returns VTQ_ERR_TIMEOUT (and clears the flag)
+ * if a bounded device-side wait of an asynchronous call ran out since the
+ * last check. */
 vtq_status vtq_synchronize(vtq_ctx* ctx);
+/* Bound of the device-side gather arrival waits of this context (default
+ * 2 s); a wait that runs out gives up, flags VTQ_ERR_TIMEOUT and leaves the
+ * GPU and the context usable. No reference counterpart. */
+vtq_status vtq_set_wait_limit(vtq_ctx* ctx, uint64_t ns);
 
 /* Upload rows [row_begin, row_end) of a row-major GGUF weight matrix
  * (QuantTensor bytes, src/model/quant_weights.rs:47-52; shape [out][in] in
@@ -133,7 +142,7 @@ vtq_status vtq_linear_q4_0(vtq_ctx* ctx, const float* x, const uint8_t* w, size_
                            size_t batch, size_t in_feat, size_t out_feat);
 
 /* ---- Context-free device API (for embedding in a host that owns memory and
- * streams). No allocation inside. ---- */
+ * streams). ---- */
 
 /* Bytes of the device layout for `rows` rows (rows re-pitched to 16 B, plus
  * a 16-byte tail pad). -1 if in_feat is invalid for dtype. No reference
@@ -145,11 +154,28 @@ vtq_status vtq_device_repack(int32_t dtype, int64_t in_feat, int64_t rows, const
                              uint8_t* dst_dev, void* cuda_stream);
 /* Same arithmetic as vtq_linear on device pointers, async on `cuda_stream`.
  * w_dev: device layout from vtq_device_repack. status_dev: optional device
- * word; kernels OR in 1 if a bounded wait timed out. */
+ * word; kernels OR in 1 if a bounded wait timed out.
+ * Allocation: none, except for integer Q4_K at batch >= 16 (the tensor-core
+ * path), whose quantised activations live in a library buffer cached per
+ * (device, stream): allocated with cudaMalloc on first use, grown when a
+ * larger batch comes, freed when the library is unloaded. Callers that must
+ * not allocate use vtq_linear_device_ws. */
 vtq_status vtq_linear_device(int32_t dtype, const uint8_t* w_dev, int64_t in_feat, int64_t rows,
                              const float* x_dev, int64_t ldx, float* y_dev, int64_t ldy,
                              int64_t batch, uint32_t flags, uint32_t* status_dev,
                              void* cuda_stream);
+/* Bytes of caller workspace vtq_linear_device_ws needs for this linear (0 when
+ * the kernel needs none: every dtype and batch except integer Q4_K at batch
+ * >= 16). No reference counterpart. */
+size_t vtq_linear_device_workspace_bytes(int32_t dtype, int64_t in_feat, int64_t batch,
+                                         uint32_t flags);
+/* vtq_linear_device with caller-owned scratch (256-byte aligned, at least
+ * vtq_linear_device_workspace_bytes); allocates nothing. Work queued on one
+ * workspace must be ordered (one stream, or the caller's events). */
+vtq_status vtq_linear_device_ws(int32_t dtype, const uint8_t* w_dev, int64_t in_feat, int64_t rows,
+                                const float* x_dev, int64_t ldx, float* y_dev, int64_t ldy,
+                                int64_t batch, uint32_t flags, uint32_t* status_dev,
+                                void* workspace, size_t workspace_bytes, void* cuda_stream);
 
 /* Q4_K / Q6_K integer linear with host x and y that allocates nothing: for
  * callers that cannot call cudaMalloc (their device memory is owned by a pool
@@ -239,8 +265,10 @@ int vtq_libm_sweep_device(const float* in, size_t n, float* out);
  * computes this rank's rows [row0, row0 + rows) of y = W x and stores them into
  * the full y of every rank over NVLink, then signals every rank once;
  * vtq_gather_wait holds the context's stream until `signals` more rank
- * launches have arrived (one per rank per gathered linear). Waits are bounded
- * (2 s) and report VTQ_ERR_TIMEOUT through the context status. */
+ * launches have arrived (one per rank per signalling gathered linear; a launch
+ * with VTQ_GATHER_DEFER does not signal, the next signalling one covers it).
+ * Waits are bounded (vtq_set_wait_limit, 2 s by default) and report
+ * VTQ_ERR_TIMEOUT through the context status (vtq_synchronize). */
 typedef struct vtq_gather vtq_gather;
 vtq_status vtq_gather_create(vtq_ctx* ctx, int32_t world, int32_t rank, size_t y_floats,
                              vtq_gather** out, uint8_t* ipc_handle /* 64 bytes */);
@@ -256,6 +284,14 @@ vtq_status vtq_gather_wait(vtq_ctx* ctx, vtq_gather* g, uint32_t signals);
 vtq_status vtq_linear_gather_wait(vtq_ctx* ctx, const vtq_weight* w, const float* x,
                                   int64_t batch, vtq_gather* g, int64_t y_offset, int64_t ldy,
                                   int64_t row0, uint32_t flags, uint32_t wait_signals);
+/* vtq_linear_list over row shards: every item's y must lie in this rank's
+ * gather buffer (vtq_gather_y(g) + offset); one persistent launch computes the
+ * items in order, stores each item's rows into every rank's buffer, and
+ * signals every rank ONCE per launch. wait_signals > 0: the launch ends once
+ * that many more rank arrivals have reached this rank (e.g. world, one launch
+ * later, to let ranks run one launch apart). */
+vtq_status vtq_linear_list_gather(vtq_ctx* ctx, const vtq_list_item* items, int32_t n,
+                                  vtq_gather* g, uint32_t flags, uint32_t wait_signals);
 vtq_status vtq_gather_destroy(vtq_gather* g);
 
 #ifdef __cplusplus

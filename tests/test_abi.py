@@ -75,3 +75,12 @@ def test_synthetic_generators_are_deterministic_and_well_formed():
     assert np.isfinite(deq).all()
     x = synth.activation("x", 2, 300)
     assert x.dtype == np.float32 and abs(float(x.mean())) < 0.2 and 0.8 < float(x.std()) < 1.2
+
+
+def test_workspace_query_without_gpu():
+    """Only integer Q4_K at batch >= 16 (the tensor-core path, sized on the
+    GPU test side) needs scratch; every other linear needs none."""
+    lib = vtq.load_library()
+    assert lib.vtq_linear_device_workspace_bytes(vtq.Q4_K, 4096, 1, 0) == 0
+    assert lib.vtq_linear_device_workspace_bytes(vtq.Q6_K, 4096, 32, 0) == 0
+    assert lib.vtq_linear_device_workspace_bytes(vtq.Q4_K, 4096, 32, vtq.Q4K_FLOAT) == 0

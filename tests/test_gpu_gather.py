@@ -54,6 +54,18 @@ def _rank(rank, port, q):
                 got = out[offs[i]:offs[i] + r]
                 if not np.array_equal(got.view(np.uint32), refs[i].view(np.uint32)):
                     raise AssertionError(f"rank {rank} step {step} matrix {i}: gathered y differs")
+        # The list form: one launch over every shard, one arrival signal per
+        # launch, each launch waiting for the previous launch's arrivals.
+        items = [(ws[i][0], xs[i].data_ptr(), offs[i] + ws[i][1]) for i in range(len(SHAPES))]
+        for step in range(3):
+            gat.linear_list(items, wait_signals=WORLD if step > 0 else 0)
+        gat.wait(WORLD)
+        ctx.synchronize()
+        out = vtq._device_floats(gat.y_ptr, total)
+        for i, (dt, n, r) in enumerate(SHAPES):
+            got = out[offs[i]:offs[i] + r]
+            if not np.array_equal(got.view(np.uint32), refs[i].view(np.uint32)):
+                raise AssertionError(f"rank {rank} list launch matrix {i}: gathered y differs")
         dist.barrier()
         gat.close()
         dist.destroy_process_group()

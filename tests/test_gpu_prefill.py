@@ -87,3 +87,31 @@ def test_config5_wk_full_size(ctx):
     got = ctx.linear(wt, x, batch)
     ref = O.linear("q4_k_integer", x, w, batch, n, r, 32)
     assert_bits(got, ref)
+
+
+def test_device_api_with_caller_workspace(ctx):
+    """vtq_linear_device_ws: the batched Q4_K path on caller-owned scratch gives
+    the same bits as vtq_linear, and a too-small workspace is rejected."""
+    import torch
+    lib = vtq.load_library()
+    n, r, b = 2048, 200, 40
+    w = synth.weight(vtq.Q4_K, "ws.w", r, n)
+    x = synth.activation("ws.x", b, n)
+    ref = ctx.linear(ctx.upload(vtq.Q4_K, w, n, r), x, b)
+    raw = torch.from_numpy(w).cuda()
+    dst = torch.empty(lib.vtq_device_layout_bytes(vtq.Q4_K, n, r), dtype=torch.uint8, device="cuda")
+    st = torch.cuda.current_stream().cuda_stream
+    assert lib.vtq_device_repack(vtq.Q4_K, n, r, raw.data_ptr(), dst.data_ptr(), st) == vtq.OK
+    need = lib.vtq_linear_device_workspace_bytes(vtq.Q4_K, n, b, 0)
+    assert need >= b * n + b * (n // 256) * 4
+    ws = torch.empty(need, dtype=torch.uint8, device="cuda")
+    dx = torch.from_numpy(x).cuda()
+    dy = torch.empty(b * r, device="cuda")
+    assert lib.vtq_linear_device_ws(vtq.Q4_K, dst.data_ptr(), n, r, dx.data_ptr(), n,
+                                    dy.data_ptr(), r, b, 0, None, ws.data_ptr(), need - 256,
+                                    st) == vtq.ERR_INVALID_ARG
+    assert lib.vtq_linear_device_ws(vtq.Q4_K, dst.data_ptr(), n, r, dx.data_ptr(), n,
+                                    dy.data_ptr(), r, b, 0, None, ws.data_ptr(), need,
+                                    st) == vtq.OK
+    torch.cuda.synchronize()
+    assert np.array_equal(dy.cpu().numpy().view(np.uint32), ref.view(np.uint32))

@@ -16,31 +16,32 @@ namespace vtq {
 namespace {
 
 __global__ void gather_wait_kernel(const unsigned* cnt, unsigned* expected, unsigned signals,
-                                   unsigned* status) {
+                                   unsigned* status, uint64_t limit_ns) {
   // Programmatic launch: wait for this rank's gathered launches to finish,
   // let the next kernel start streaming its weights, then wait for the peers.
   asm volatile("griddepcontrol.wait;" ::: "memory");
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   if (threadIdx.x != 0) return;
   const unsigned target = *expected + signals;
-  *expected = target;
   const uint64_t t0 = globaltimer();
   for (;;) {
     unsigned v;
     asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(cnt) : "memory");
     if ((int)(v - target) >= 0) break;  // wrap-safe comparison
-    if (globaltimer() - t0 > VTQ_WAIT_LIMIT_NS) {
+    if (globaltimer() - t0 > limit_ns) {
+      // Give up: report, and count none of the missing arrivals as consumed.
       record_error(status, KERR_TIMEOUT);
-      break;
+      return;
     }
   }
+  *expected = target;
   __threadfence_system();
 }
 
 }  // namespace
 
 cudaError_t launch_gather_wait(unsigned* cnt, unsigned* expected, unsigned signals,
-                               unsigned* status, cudaStream_t st) {
+                               unsigned* status, cudaStream_t st, uint64_t limit_ns) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(1);
   cfg.blockDim = dim3(32);
@@ -51,7 +52,7 @@ cudaError_t launch_gather_wait(unsigned* cnt, unsigned* expected, unsigned signa
   cfg.attrs = attr;
   cfg.numAttrs = pdl_enabled() ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, gather_wait_kernel, (const unsigned*)cnt, expected, signals,
-                            status);
+                            status, limit_ns);
 }
 
 }  // namespace vtq

@@ -524,6 +524,15 @@ struct Scratch {
 std::mutex g_scratch_mu;
 std::map<std::pair<int, cudaStream_t>, Scratch> g_scratch;
 std::vector<uint8_t*> g_scratch_retired;
+// Release every cached buffer when the library is unloaded (errors ignored:
+// the CUDA context may already be gone at that point).
+struct ScratchReaper {
+  ~ScratchReaper() {
+    for (auto& kv : g_scratch)
+      if (kv.second.ptr) cudaFree(kv.second.ptr);
+    for (uint8_t* p : g_scratch_retired) cudaFree(p);
+  }
+} g_scratch_reaper;
 
 cudaError_t scratch(size_t bytes, cudaStream_t st, uint8_t** out) {
   int dev = 0;
@@ -566,14 +575,25 @@ bool kq_gemm_supported(const DevMatrix& m, int64_t batch) {
          (int64_t)SMEM_BYTES <= max_smem_optin();
 }
 
+size_t kq_gemm_workspace_bytes(int64_t in_feat, int64_t batch) {
+  const size_t xq_bytes = ((size_t)batch * in_feat + 1023) & ~(size_t)1023;
+  return xq_bytes + (size_t)batch * (in_feat / 256) * 4;
+}
+
 cudaError_t launch_kq_gemm(const DevMatrix& m, const float* x, int64_t ldx, int64_t batch, float* y,
-                           int64_t ldy, unsigned* status, cudaStream_t st) {
+                           int64_t ldy, unsigned* status, cudaStream_t st, uint8_t* ws,
+                           size_t ws_bytes) {
   if (!kq_gemm_supported(m, batch)) return cudaErrorInvalidValue;
   const int n = (int)m.in_feat, S = n / 256, M = (int)batch, R = (int)m.out_feat;
   const size_t xq_bytes = ((size_t)M * n + 1023) & ~(size_t)1023;
-  uint8_t* buf = nullptr;
-  cudaError_t e = scratch(xq_bytes + (size_t)M * S * 4, st, &buf);
-  if (e != cudaSuccess) return e;
+  const size_t need = kq_gemm_workspace_bytes(n, M);
+  uint8_t* buf = ws;
+  cudaError_t e = cudaSuccess;
+  if (ws) {
+    if (ws_bytes < need || (reinterpret_cast<uintptr_t>(ws) & 255u)) return cudaErrorInvalidValue;
+  } else if ((e = scratch(need, st, &buf)) != cudaSuccess) {
+    return e;
+  }
   int8_t* xq = reinterpret_cast<int8_t*>(buf);
   float* xd = reinterpret_cast<float*>(buf + xq_bytes);
   {

@@ -55,6 +55,7 @@ struct KqLItem {
   float* y;
   int pitch, R, S, qt, lpr, nch, rps, rows_base, rows_rem, wait_for, signal;
   int qbase;  // first global block index of this item's pre-quantisation (-1: dependent item)
+  int send;   // gathered list: this item's rows go to the other ranks (last item writing its y)
 };
 
 // Global record of one item's quantised activation: [xd | bsum | xq], the
@@ -74,6 +75,7 @@ struct KqListParams {
   uint8_t* xrec;  // KQ_LIST_MAX records of KQ_LIST_REC bytes
   unsigned* hstatus;  // optional host-mapped word: the last CTA copies *status there
   int nq;         // blocks to pre-quantise (sum of S over independent items)
+  KqListGather g;  // g.world > 0: every y row also goes to every other rank
 };
 
 __device__ __forceinline__ void consumer_sync() {
@@ -356,6 +358,23 @@ __global__ void __launch_bounds__((CWL + 1) * 32, 1) kq_list_kernel(const __grid
     }
   }
   consumer_sync();
+  if (P.g.world > 0) {
+    // Row-sharded list: this CTA's finished rows of every item go to every
+    // other rank's copy of y (contiguous rows, coalesced stores over NVLink;
+    // no multicast). Rows were stored to this rank's y by other warps of the
+    // CTA before the barrier above.
+    for (int job = warp; job < P.n * P.g.world; job += CWL) {
+      const int i = job / P.g.world, q = job - i * P.g.world;
+      const KqLItem& it = P.it[i];
+      if (q == P.g.rank || !it.send) continue;
+      const int r0 = bid * it.rows_base + min(bid, it.rows_rem);
+      const int nrows = it.rows_base + (bid < it.rows_rem ? 1 : 0);
+      const float* src = it.y + r0;
+      float* dst = reinterpret_cast<float*>(reinterpret_cast<char*>(it.y + r0) + P.g.peer_off[q]);
+      for (int e = lane; e < nrows; e += 32) dst[e] = src[e];
+    }
+    consumer_sync();
+  }
   if (tid == 0) {
     unsigned prev;
     asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;"
@@ -366,6 +385,32 @@ __global__ void __launch_bounds__((CWL + 1) * 32, 1) kq_list_kernel(const __grid
       for (int i = 0; i < P.n; i++) P.cnt[i] = 0;
       P.cnt[KQ_LIST_MAX] = 0;
       P.cnt[KQ_LIST_MAX + 1] = 0;
+      if (P.g.world > 0) {
+        // Every CTA's stores reached this thread through the acq_rel chain
+        // on the exit counter; one system-scope fence covers them all before
+        // the arrival signals. Then, if asked, wait for the other ranks.
+        __threadfence_system();
+        for (int q = 0; q < P.g.world; q++)
+          asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(P.g.cnt[q]) : "memory");
+        if (P.g.wait_signals) {
+          const unsigned target = *P.g.expected + P.g.wait_signals;
+          const uint64_t t0 = globaltimer();
+          bool ok = true;
+          for (;;) {
+            unsigned v;
+            asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(P.g.my_cnt)
+                         : "memory");
+            if ((int)(v - target) >= 0) break;
+            if (globaltimer() - t0 > P.g.limit_ns) {
+              record_error(P.status, KERR_TIMEOUT);
+              ok = false;  // the missing arrivals are not counted as consumed
+              break;
+            }
+          }
+          if (ok) *P.g.expected = target;
+          __threadfence_system();
+        }
+      }
       // Completion word for a host that reads y in place: it holds a sentinel
       // until this store, so a launch that never got here reads as failed.
       if (P.hstatus) *reinterpret_cast<volatile unsigned*>(P.hstatus) = P.status ? *P.status : 0u;
@@ -378,11 +423,17 @@ static inline uint32_t align_up(uint32_t v, uint32_t a) { return (v + a - 1) / a
 }  // namespace
 
 cudaError_t launch_kq_list(const KqListItem* items, int n, unsigned* counters, uint8_t* xrec,
-                           unsigned* status, cudaStream_t st, unsigned* hstatus) {
+                           unsigned* status, cudaStream_t st, unsigned* hstatus,
+                           const KqListGather* g) {
   if (n < 1 || n > KQ_LIST_MAX || !counters || !xrec) return cudaErrorInvalidValue;
   KqListParams P{};
   P.n = n;
   P.hstatus = hstatus;
+  if (g) {
+    if (g->world < 1 || g->world > kMaxRanks || g->rank < 0 || g->rank >= g->world)
+      return cudaErrorInvalidValue;
+    P.g = *g;
+  }
   P.cnt = counters;
   P.xrec = xrec;
   P.status = status;
@@ -421,8 +472,13 @@ cudaError_t launch_kq_list(const KqListItem* items, int n, unsigned* counters, u
     it.qbase = it.wait_for < 0 ? nq : -1;
     if (it.wait_for < 0) nq += it.S;
   }
-  for (int i = 0; i < n; i++)
+  for (int i = 0; i < n; i++) {
     if (P.it[i].wait_for >= 0) P.it[P.it[i].wait_for].signal = 1;
+    // Only the last item that writes a given y sends it to the other ranks.
+    P.it[i].send = 1;
+    for (int j = i + 1; j < n; j++)
+      if (items[j].y == items[i].y && items[j].m.out_feat == items[i].m.out_feat) P.it[i].send = 0;
+  }
   P.nq = nq;
   uint32_t xbytes = 0;  // one activation buffer: the largest record of the list
   for (int i = 0; i < n; i++)

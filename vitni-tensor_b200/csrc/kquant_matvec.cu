@@ -241,7 +241,7 @@ __global__ void __launch_bounds__((CW + 1) * 32, VTQ_KQ_CTAS) kq_matvec_kernel(c
       // into the last one, whose system-scope fence then covers all of them
       // before the arrival signals (causality order is transitive).
       __syncwarp();
-      if (lane == 0) {
+      if (lane == 0 && p.g.signal) {
         unsigned prev;
         asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(prev) : "l"(p.g.done)
                      : "memory");
@@ -253,18 +253,20 @@ __global__ void __launch_bounds__((CW + 1) * 32, VTQ_KQ_CTAS) kq_matvec_kernel(c
             if (q < p.g.world) atomicAdd_system(p.g.cnt[q], 1u);
           if (p.g.wait_signals) {
             const unsigned target = *p.g.expected + p.g.wait_signals;
-            *p.g.expected = target;
             const uint64_t t0 = globaltimer();
+            bool ok = true;
             for (;;) {
               unsigned v;
               asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p.g.my_cnt)
                            : "memory");
               if ((int)(v - target) >= 0) break;
-              if (globaltimer() - t0 > VTQ_WAIT_LIMIT_NS) {
+              if (globaltimer() - t0 > p.g.limit_ns) {
                 record_error(p.status, KERR_TIMEOUT);
+                ok = false;  // the missing arrivals are not counted as consumed
                 break;
               }
             }
+            if (ok) *p.g.expected = target;
             __threadfence_system();
           }
         }

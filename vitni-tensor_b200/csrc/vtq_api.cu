@@ -29,6 +29,9 @@ struct vtq_ctx {
   unsigned* list_cnt = nullptr;  // completion counters of vtq_linear_list (zeroed, left zeroed)
   uint8_t* list_rec = nullptr;   // vtq_linear_list's quantised activations (KQ_LIST_MAX records)
   unsigned* hstat = nullptr;     // page-locked completion word of in-place host-pointer lists
+  uint64_t wait_limit_ns = 2000000000ull;  // bound of the gather arrival waits
+  uint8_t* ws = nullptr;  // batched (tensor-core) linears' quantised activations
+  size_t ws_cap = 0;
   std::string err;
 };
 
@@ -91,14 +94,37 @@ const int64_t kGemmMinBatch = [] {
 }();
 
 // Launch the kernel that implements dtype's linear_dispatch arm.
+bool uses_gemm(const DevMatrix& m, int64_t batch, uint32_t flags) {
+  return m.dtype == T_Q4_K && !(flags & VTQ_Q4K_FLOAT) && batch >= kGemmMinBatch &&
+         kq_gemm_supported(m, batch);
+}
+
 cudaError_t run_linear(const DevMatrix& m, const float* x, int64_t ldx, float* y, int64_t ldy,
-                       int64_t batch, uint32_t flags, unsigned* status, cudaStream_t st) {
-  if (m.dtype == T_Q4_K && !(flags & VTQ_Q4K_FLOAT) && batch >= kGemmMinBatch &&
-      kq_gemm_supported(m, batch))
-    return launch_kq_gemm(m, x, ldx, batch, y, ldy, status, st);
+                       int64_t batch, uint32_t flags, unsigned* status, cudaStream_t st,
+                       uint8_t* ws = nullptr, size_t ws_bytes = 0) {
+  if (uses_gemm(m, batch, flags))
+    return launch_kq_gemm(m, x, ldx, batch, y, ldy, status, st, ws, ws_bytes);
   if (m.dtype == T_Q6_K || (m.dtype == T_Q4_K && !(flags & VTQ_Q4K_FLOAT)))
     return launch_kq_matvec(m, x, ldx, batch, y, ldy, status, st);
   return launch_canon_matvec(m, x, ldx, batch, y, ldy, status, st);
+}
+
+// The context's workspace for a batched linear, grown (after the stream has
+// drained) when a larger batch arrives; freed with the context.
+vtq_status ensure_ws(vtq_ctx* c, const DevMatrix& m, int64_t batch, uint32_t flags) {
+  if (!uses_gemm(m, batch, flags)) return VTQ_OK;
+  const size_t need = kq_gemm_workspace_bytes(m.in_feat, batch);
+  if (need <= c->ws_cap) return VTQ_OK;
+  const size_t cap = (std::max(need, c->ws_cap * 2) + 4095) / 4096 * 4096;
+  if (c->ws) {
+    VTQ_CUDA(c, cudaStreamSynchronize(c->stream));
+    cudaFree(c->ws);
+    c->ws = nullptr;
+    c->ws_cap = 0;
+  }
+  VTQ_CUDA(c, cudaMalloc(&c->ws, cap));
+  c->ws_cap = cap;
+  return VTQ_OK;
 }
 
 // Kernel-side limits (shared-memory residency of one activation row set).
@@ -188,7 +214,9 @@ vtq_status linear_host(vtq_ctx* c, const DevMatrix& m, const float* x, float* y,
     memcpy(c->hio + xoff, x, xbytes);
     VTQ_CUDA(c, cudaMemcpyAsync(dx, c->hio + xoff, xbytes, cudaMemcpyHostToDevice, c->stream));
   }
-  VTQ_CUDA(c, run_linear(m, dx, m.in_feat, dy, m.out_feat, batch, flags, dstat, c->stream));
+  if (vtq_status s = ensure_ws(c, m, batch, flags)) return s;
+  VTQ_CUDA(c, run_linear(m, dx, m.in_feat, dy, m.out_feat, batch, flags, dstat, c->stream, c->ws,
+                         c->ws_cap));
   uint32_t statbuf[kStatusBytes / 4];
   if (y_pinned) {
     VTQ_CUDA(c, cudaMemcpyAsync(c->hio, c->io, kStatusBytes, cudaMemcpyDeviceToHost, c->stream));
@@ -322,6 +350,7 @@ vtq_status vtq_destroy(vtq_ctx* c) {
   if (c->io) cudaFree(c->io);
   if (c->list_cnt) cudaFree(c->list_cnt);
   if (c->list_rec) cudaFree(c->list_rec);
+  if (c->ws) cudaFree(c->ws);
   if (c->hstat) cudaFreeHost(c->hstat);
   if (c->hio) cudaFreeHost(c->hio);
   if (c->done) cudaEventDestroy(c->done);
@@ -342,6 +371,22 @@ vtq_status vtq_synchronize(vtq_ctx* c) {
   if (!c) return VTQ_ERR_INVALID_ARG;
   VTQ_CUDA(c, cudaSetDevice(c->device));
   VTQ_CUDA(c, cudaStreamSynchronize(c->stream));
+  // Errors of asynchronous calls surface here: a bounded device wait that ran
+  // out left a flag in the context's status word.
+  unsigned st = 0;
+  VTQ_CUDA(c, cudaMemcpyAsync(&st, c->io, 4, cudaMemcpyDeviceToHost, c->stream));
+  VTQ_CUDA(c, cudaStreamSynchronize(c->stream));
+  if (st != 0) {
+    VTQ_CUDA(c, cudaMemsetAsync(c->io, 0, 4, c->stream));
+    VTQ_CUDA(c, cudaStreamSynchronize(c->stream));
+    return fail(c, VTQ_ERR_TIMEOUT, "a device-side wait timed out");
+  }
+  return VTQ_OK;
+}
+
+vtq_status vtq_set_wait_limit(vtq_ctx* c, uint64_t ns) {
+  if (!c || ns == 0) return fail(c, VTQ_ERR_INVALID_ARG, "vtq_set_wait_limit: limit must be > 0");
+  c->wait_limit_ns = ns;
   return VTQ_OK;
 }
 
@@ -393,8 +438,9 @@ vtq_status vtq_linear(vtq_ctx* c, const vtq_weight* w, const float* x, float* y,
   VTQ_CUDA(c, cudaSetDevice(c->device));
   if (flags & VTQ_PTR_HOST) return linear_host(c, w->m, x, y, batch, flags);
   if (vtq_status s = check_kernel_limits(c, w->m, flags)) return s;
+  if (vtq_status s = ensure_ws(c, w->m, batch, flags)) return s;
   VTQ_CUDA(c, run_linear(w->m, x, w->m.in_feat, y, w->m.out_feat, batch, flags,
-                         reinterpret_cast<unsigned*>(c->io), c->stream));
+                         reinterpret_cast<unsigned*>(c->io), c->stream, c->ws, c->ws_cap));
   return VTQ_OK;
 }
 
@@ -579,6 +625,36 @@ vtq_status vtq_device_repack(int32_t dtype, int64_t in_feat, int64_t rows, const
   return VTQ_OK;
 }
 
+size_t vtq_linear_device_workspace_bytes(int32_t dtype, int64_t in_feat, int64_t batch,
+                                         uint32_t flags) {
+  const int64_t rb = packed_row_bytes(dtype, in_feat);
+  if (rb < 0 || batch < 0) return 0;
+  DevMatrix m{dtype, in_feat, 1, rb, device_pitch(dtype, in_feat), nullptr};
+  return uses_gemm(m, batch, flags) ? kq_gemm_workspace_bytes(in_feat, batch) : 0;
+}
+
+vtq_status vtq_linear_device_ws(int32_t dtype, const uint8_t* w_dev, int64_t in_feat, int64_t rows,
+                                const float* x_dev, int64_t ldx, float* y_dev, int64_t ldy,
+                                int64_t batch, uint32_t flags, uint32_t* status_dev,
+                                void* workspace, size_t workspace_bytes, void* s) {
+  if (!dtype_supported(dtype)) return VTQ_ERR_NOT_IMPLEMENTED;
+  const int64_t rb = packed_row_bytes(dtype, in_feat);
+  if (rb < 0 || rows < 0 || batch < 0 || ldx < in_feat || ldy < rows) return VTQ_ERR_INTERNAL;
+  if (batch == 0 || rows == 0) return VTQ_OK;
+  if (!w_dev || !x_dev || !y_dev) return VTQ_ERR_INVALID_ARG;
+  if (in_feat > 32768) return VTQ_ERR_NOT_IMPLEMENTED;
+  if (reinterpret_cast<uintptr_t>(w_dev) & 15u) return VTQ_ERR_INVALID_ARG;
+  DevMatrix m{dtype, in_feat, rows, rb, device_pitch(dtype, in_feat), w_dev};
+  const size_t need = uses_gemm(m, batch, flags) ? kq_gemm_workspace_bytes(in_feat, batch) : 0;
+  if (need && (!workspace || workspace_bytes < need ||
+               (reinterpret_cast<uintptr_t>(workspace) & 255u)))
+    return VTQ_ERR_INVALID_ARG;
+  if (run_linear(m, x_dev, ldx, y_dev, ldy, batch, flags, status_dev, static_cast<cudaStream_t>(s),
+                 static_cast<uint8_t*>(workspace), workspace_bytes) != cudaSuccess)
+    return VTQ_ERR_GPU;
+  return VTQ_OK;
+}
+
 vtq_status vtq_linear_device(int32_t dtype, const uint8_t* w_dev, int64_t in_feat, int64_t rows,
                              const float* x_dev, int64_t ldx, float* y_dev, int64_t ldy,
                              int64_t batch, uint32_t flags, uint32_t* status_dev, void* s) {
@@ -687,6 +763,10 @@ vtq_status vtq_linear_gather_wait(vtq_ctx* c, const vtq_weight* w, const float* 
   t.my_cnt = reinterpret_cast<unsigned*>(g->base);
   t.expected = reinterpret_cast<unsigned*>(g->base + 4);
   t.wait_signals = wait_signals;
+  t.signal = (flags & VTQ_GATHER_DEFER) ? 0 : 1;
+  t.limit_ns = c->wait_limit_ns;
+  if (!t.signal && wait_signals)
+    return fail(c, VTQ_ERR_INVALID_ARG, "vtq_linear_gather: a deferred launch cannot wait");
   VTQ_CUDA(c, launch_kq_matvec(m, x, m.in_feat, batch, nullptr, 0,
                                reinterpret_cast<unsigned*>(c->io), c->stream, &t));
   return VTQ_OK;
@@ -703,7 +783,54 @@ vtq_status vtq_gather_wait(vtq_ctx* c, vtq_gather* g, uint32_t signals) {
   VTQ_CUDA(c, cudaSetDevice(c->device));
   VTQ_CUDA(c, launch_gather_wait(reinterpret_cast<unsigned*>(g->base),
                                  reinterpret_cast<unsigned*>(g->base + 4), signals,
-                                 reinterpret_cast<unsigned*>(c->io), c->stream));
+                                 reinterpret_cast<unsigned*>(c->io), c->stream,
+                                 c->wait_limit_ns));
+  return VTQ_OK;
+}
+
+vtq_status vtq_linear_list_gather(vtq_ctx* c, const vtq_list_item* items, int32_t n,
+                                  vtq_gather* g, uint32_t flags, uint32_t wait_signals) {
+  if (!c || !g || (!items && n)) return fail(c, VTQ_ERR_INVALID_ARG, "null argument");
+  if (n < 1 || n > VTQ_LIST_MAX)
+    return fail(c, VTQ_ERR_INVALID_ARG, "vtq_linear_list_gather: 1..VTQ_LIST_MAX items");
+  if (flags & (VTQ_PTR_HOST | VTQ_Q4K_FLOAT))
+    return fail(c, VTQ_ERR_NOT_IMPLEMENTED,
+                "vtq_linear_list_gather: not implemented (device pointers, integer regime only)");
+  for (int q = 0; q < g->world; q++)
+    if (!g->peer[q])
+      return fail(c, VTQ_ERR_INVALID_ARG, "vtq_linear_list_gather: gather not connected");
+  const float* ybeg = reinterpret_cast<const float*>(g->base + kGatherHdr);
+  const float* yend = ybeg + g->y_floats;
+  KqListItem it[KQ_LIST_MAX];
+  for (int i = 0; i < n; i++) {
+    const vtq_list_item& s = items[i];
+    if (!s.w || !s.x || !s.y)
+      return fail(c, VTQ_ERR_INVALID_ARG, "vtq_linear_list_gather: null item field");
+    if (s.w->m.dtype != T_Q4_K && s.w->m.dtype != T_Q6_K)
+      return fail(c, VTQ_ERR_NOT_IMPLEMENTED,
+                  "vtq_linear_list_gather: not implemented (weight dtype not Q4_K / Q6_K)");
+    if (s.wait_for < -1 || s.wait_for >= i)
+      return fail(c, VTQ_ERR_INVALID_ARG, "vtq_linear_list_gather: wait_for must name an earlier item");
+    if (s.y < ybeg || s.y + s.w->m.out_feat > yend)
+      return fail(c, VTQ_ERR_INVALID_ARG,
+                  "vtq_linear_list_gather: y must lie in this rank's gather buffer");
+    if (vtq_status st = check_kernel_limits(c, s.w->m, 0)) return st;
+    it[i] = KqListItem{s.w->m, s.x, s.y, s.wait_for};
+  }
+  KqListGather lg;
+  lg.world = g->world;
+  lg.rank = g->rank;
+  for (int q = 0; q < g->world; q++) {
+    lg.peer_off[q] = g->peer[q] - g->base;
+    lg.cnt[q] = reinterpret_cast<unsigned*>(g->peer[q]);
+  }
+  lg.my_cnt = reinterpret_cast<unsigned*>(g->base);
+  lg.expected = reinterpret_cast<unsigned*>(g->base + 4);
+  lg.wait_signals = wait_signals;
+  lg.limit_ns = c->wait_limit_ns;
+  VTQ_CUDA(c, cudaSetDevice(c->device));
+  VTQ_CUDA(c, launch_kq_list(it, n, c->list_cnt, c->list_rec, reinterpret_cast<unsigned*>(c->io),
+                             c->stream, nullptr, &lg));
   return VTQ_OK;
 }
 

@@ -49,6 +49,11 @@ struct GatherTarget {
   unsigned* my_cnt;
   unsigned* expected;
   unsigned wait_signals;
+  // 0: this launch does not signal; a later gathered launch on the same
+  // stream signals for it (its system fence covers every earlier launch's
+  // stores, which precede it in stream order).
+  int signal = 1;
+  uint64_t limit_ns = 2000000000ull;  // bound of the arrival wait
 };
 
 // Transform applied to a batch-1 activation row while the matvec quantises it
@@ -94,22 +99,44 @@ struct KqListItem {
   float* y;
   int wait_for;
 };
+// Row-sharded list: every item's y lies in this rank's gather buffer; the
+// launch also stores its rows into every other rank's buffer (at byte offset
+// peer_off[q] from this rank's) and, once all CTAs have, signals every
+// rank's arrival counter once; wait_signals > 0 makes it then wait (bounded
+// by limit_ns) until that many more arrivals have reached this rank.
+struct KqListGather {
+  int world = 0, rank = 0;
+  int64_t peer_off[kMaxRanks] = {};
+  unsigned* cnt[kMaxRanks] = {};
+  unsigned* my_cnt = nullptr;
+  unsigned* expected = nullptr;
+  unsigned wait_signals = 0;
+  uint64_t limit_ns = 2000000000ull;
+};
 // `hstatus` (optional, host-mapped): receives the status word once the whole
 // launch has finished (for callers that read y straight from host memory).
 cudaError_t launch_kq_list(const KqListItem* items, int n, unsigned* counters, uint8_t* xrec,
-                           unsigned* status, cudaStream_t st, unsigned* hstatus = nullptr);
+                           unsigned* status, cudaStream_t st, unsigned* hstatus = nullptr,
+                           const KqListGather* g = nullptr);
 
 // Waits on `st` until this rank's arrival counter has received `signals` more
 // arrivals than before (`expected` is a device counter of arrivals consumed).
-// Bounded: after 2 s the status word gets KERR_TIMEOUT.
+// Bounded: after limit_ns the status word gets KERR_TIMEOUT and the consumed
+// count is left unchanged (the missing arrivals are not counted as seen).
 cudaError_t launch_gather_wait(unsigned* cnt, unsigned* expected, unsigned signals,
-                               unsigned* status, cudaStream_t st);
+                               unsigned* status, cudaStream_t st,
+                               uint64_t limit_ns = 2000000000ull);
 
 // Batched integer Q4_K linear on the tensor cores (tcgen05 kind::i8): same
 // results as launch_kq_matvec for any batch; used for prefill-sized batches.
+// Scratch: the quantised activations (kq_gemm_workspace_bytes). With ws ==
+// nullptr the launcher uses a buffer cached per (device, stream), allocated
+// on first use and grown with cudaMalloc, freed when the library unloads.
 bool kq_gemm_supported(const DevMatrix& m, int64_t batch);
+size_t kq_gemm_workspace_bytes(int64_t in_feat, int64_t batch);
 cudaError_t launch_kq_gemm(const DevMatrix& m, const float* x, int64_t ldx, int64_t batch,
-                           float* y, int64_t ldy, unsigned* status, cudaStream_t st);
+                           float* y, int64_t ldy, unsigned* status, cudaStream_t st,
+                           uint8_t* ws = nullptr, size_t ws_bytes = 0);
 
 // Canonical fp32 matvec (8 pinned lanes, 8192-element chunks, fixed trees)
 // for Q8_0 / Q5_0 / Q4_0 / F32 rows and the float-fused Q4_K mode.

@@ -41,7 +41,8 @@ EXPORTS = (
     "vtq_gather_create", "vtq_gather_connect", "vtq_gather_y", "vtq_linear_gather",
     "vtq_gather_wait", "vtq_gather_destroy", "vtq_libm_sweep_device", "vtq_linear_gather_wait",
     "vtq_decode_timing", "vtq_decode_debug_buffer", "vtq_decode_step_kind",
-    "vtq_exact_sum_host", "vtq_exact_sum_device", "vtq_decode_launches", "vtq_linear_list",
+    "vtq_exact_sum_host", "vtq_exact_sum_device", "vtq_decode_launches", "vtq_linear_list", "vtq_set_wait_limit",
+    "vtq_linear_list_gather", "vtq_linear_device_workspace_bytes", "vtq_linear_device_ws",
 )
 
 
@@ -96,6 +97,7 @@ class ListItem(ctypes.Structure):
 
 
 LIST_MAX = 32
+GATHER_DEFER = 4
 
 
 def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
@@ -154,6 +156,11 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         "vtq_gather_destroy": (c_i32, [c_p]),
         "vtq_libm_sweep_device": (c_i32, [c_p, c_sz, c_p]),
         "vtq_linear_list": (c_i32, [c_p, c_p, c_i32, c_u32]),
+        "vtq_set_wait_limit": (c_i32, [c_p, ctypes.c_uint64]),
+        "vtq_linear_device_workspace_bytes": (c_sz, [c_i32, c_i64, c_i64, c_u32]),
+        "vtq_linear_device_ws": (c_i32, [c_i32, c_p, c_i64, c_i64, c_p, c_i64, c_p, c_i64, c_i64,
+                                         c_u32, c_p, c_p, c_sz, c_p]),
+        "vtq_linear_list_gather": (c_i32, [c_p, c_p, c_i32, c_p, c_u32, c_u32]),
         "vtq_linear_gather_wait": (c_i32, [c_p, c_p, c_p, c_i64, c_p, c_i64, c_i64, c_i64, c_u32,
                                            c_u32]),
     }
@@ -228,6 +235,10 @@ class Context:
 
     def synchronize(self):
         self._check(self.lib.vtq_synchronize(self.handle))
+
+    def set_wait_limit(self, ns: int):
+        """Bound of this context's device-side gather waits (default 2 s)."""
+        self._check(self.lib.vtq_set_wait_limit(self.handle, int(ns)))
 
     # -- resident weights -------------------------------------------------
     def upload(self, dtype: int, data, in_feat: int, out_feat: int, row_begin: int = 0,
@@ -331,6 +342,18 @@ def linear_dispatch(ctx: Context, x, w: QuantTensor, in_feat: int, out_feat: int
     return y
 
 
+def _device_floats(ptr: int, n: int) -> np.ndarray:
+    """Copy n floats from device address ptr to a new host array."""
+    out = np.empty(n, np.float32)
+    import torch
+
+    class _A:
+        __cuda_array_interface__ = {"shape": (n,), "typestr": "<f4", "data": (ptr, False),
+                                    "version": 3}
+    out[:] = torch.as_tensor(_A(), device="cuda").cpu().numpy()
+    return out
+
+
 class Gather:
     """Fused row-shard all-gather over NVLink (one per rank of a process group).
 
@@ -343,26 +366,43 @@ class Gather:
     def __init__(self, ctx: "Context", y_floats: int, group=None):
         import torch.distributed as dist
         self.ctx, self.lib = ctx, ctx.lib
-        self.world, self.rank = dist.get_world_size(group), dist.get_rank(group)
+        single = not dist.is_available() or not dist.is_initialized()
+        self.world, self.rank = (1, 0) if single else (dist.get_world_size(group),
+                                                      dist.get_rank(group))
         h = ctypes.c_void_p()
         ipc = ctypes.create_string_buffer(64)
         ctx._check(self.lib.vtq_gather_create(ctx.handle, self.world, self.rank, y_floats,
                                               ctypes.byref(h), ipc))
         self.handle = h
-        handles = [None] * self.world
-        dist.all_gather_object(handles, ipc.raw, group=group)
+        handles = [ipc.raw]
+        if not single:
+            handles = [None] * self.world
+            dist.all_gather_object(handles, ipc.raw, group=group)
         blob = b"".join(handles)
         ctx._check(self.lib.vtq_gather_connect(self.handle, blob))
         self.y_ptr = self.lib.vtq_gather_y(self.handle)
         self.y_floats = y_floats
 
     def linear(self, w: "Weight", x_ptr: int, row0: int, ldy: int, y_offset: int = 0,
-               batch: int = 1, wait_signals: int = 0):
+               batch: int = 1, wait_signals: int = 0, defer: bool = False):
         """wait_signals > 0: the launch ends only once that many rank arrivals
-        (including this launch's) have reached this rank."""
+        (including this launch's) have reached this rank. defer: no arrival
+        signal; the next signalling launch covers this one."""
         self.ctx._check(self.lib.vtq_linear_gather_wait(self.ctx.handle, w.handle, x_ptr, batch,
-                                                        self.handle, y_offset, ldy, row0, 0,
+                                                        self.handle, y_offset, ldy, row0,
+                                                        GATHER_DEFER if defer else 0,
                                                         wait_signals))
+
+    def linear_list(self, items, wait_signals: int = 0):
+        """vtq_linear_list_gather: items are (Weight, x_ptr, y_offset[, wait_for])
+        with y at y_offset floats into this rank's gather buffer; one launch,
+        one arrival signal to every rank."""
+        arr = (ListItem * len(items))()
+        for i, it in enumerate(items):
+            w, xp, yo = it[:3]
+            arr[i] = ListItem(w.handle, xp, self.y_ptr + 4 * yo, it[3] if len(it) > 3 else -1)
+        self.ctx._check(self.lib.vtq_linear_list_gather(self.ctx.handle, arr, len(items),
+                                                        self.handle, 0, wait_signals))
 
     def wait(self, signals: int):
         self.ctx._check(self.lib.vtq_gather_wait(self.ctx.handle, self.handle, signals))
