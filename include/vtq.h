@@ -187,12 +187,15 @@ vtq_status vtq_linear_device_ws(int32_t dtype, const uint8_t* w_dev, int64_t in_
  * exit): 64 + batch*in_feat + batch*rows floats must fit, else VTQ_ERR_INTERNAL.
  * All calls on a device share that array, so calls that overlap on the GPU
  * race. The first call on a device looks the array's address up; make it
- * before any stream capture. Synchronous: returns when y is written. */
+ * before any stream capture. The address is kept for the life of the process
+ * (it belongs to the device's primary context): do not call this again after
+ * a cudaDeviceReset in the same process. Synchronous: returns when y is
+ * written. */
 vtq_status vtq_linear_host_noalloc(int32_t dtype, const uint8_t* w_dev, int64_t in_feat,
                                    int64_t rows, const float* x, float* y, int64_t batch,
                                    void* cuda_stream);
 
-/* ---- Quantized decode session: a GGUF Llama or Qwen2 model resident on
+/* ---- Quantized decode session (TinyLlama-shaped decode workload): a GGUF Llama or Qwen2 model resident on
  * one device; the decode step of src/model/forward_quantized.rs:329-649 and the
  * prompt + greedy loop of src/model/inference.rs:312-327 run as one CUDA graph
  * per step with the position and current token in device memory. ---- */

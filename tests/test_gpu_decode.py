@@ -1,6 +1,6 @@
 """Device decode session vs the CPU oracle of the reference's decode step:
 per-step logits bit-exact, generated tokens and receipt digests identical
-(BASELINE config 4 and smaller models through the same code)."""
+(the TinyLlama-shaped decode workload and smaller models through the same code)."""
 import numpy as np
 import pytest
 

@@ -12,8 +12,9 @@
 // fixed_tree over the 8 lanes; the row result is fixed_tree over chunks.
 // Chunk starts are multiples of 8192, so lane = i mod 8 everywhere.
 //
-// Design: a CTA owns a tile of up to 32 output rows; 4 threads per row, thread
-// p running lanes 2p and 2p+1. Products are formed two at a time with
+// Design (Q4_K float mode, F32): a CTA owns a tile of up to 32 output rows; 4
+// threads per row, thread p running lanes 2p and 2p+1 (the block-32 formats
+// use canon_lane_kernel below: one thread per lane). Products are formed two at a time with
 // mul.rn.f32x2; every accumulation add is a scalar add.rn.f32. A packed add
 // must never consume a packed product: ptxas contracts mul.rn.f32x2 followed
 // by add/sub.rn.f32x2 into a fused multiply-add (observed with -fmad=false and
@@ -282,6 +283,150 @@ __global__ void __launch_bounds__(CN_THREADS)
   }
 }
 
+// ---- Block-32 formats (Q8_0 / Q4_0 / Q5_0): one thread per (row, lane) ----
+// Thread (r, j) runs lane j of row r: within every 32-element block it owns
+// elements j, j + 8, j + 16, j + 24, i.e. exactly the reference's lane
+// i mod 8, in ascending i. Every thread forms its own products (dequantise
+// in the reference's fp32 order, multiply, then one add.rn into the lane), so
+// a CTA of 32 rows runs 256 independent chains instead of 64.
+constexpr int CL_RMAX = 32;
+constexpr int CL_THREADS = CL_RMAX * 8;
+
+// The 4 dequantised weights of lane j in one block (block bytes at blk).
+template <int FMT>
+__device__ __forceinline__ void lane_weights(const uint8_t* blk, int j, float (&w)[4]) {
+  const float scale = h2f(lds16(blk));
+  if (FMT == T_Q8_0) {  // quant.rs:193-210: scale * (qs[k] as i8 as f32)
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+      const uint32_t u = (uint32_t)(blk[2 + j + 8 * k] ^ 0x80u);  // q + 128
+      w[k] = __fmul_rn(scale, __fsub_rn(__uint_as_float(0x4B000000u | u), 8388736.0f));
+    }
+  } else if (FMT == T_Q4_0) {  // quant.rs:91-111: scale * (nibble - 8)
+    // Nibbles interleave: element 2m is the low nibble of byte m, 2m + 1 the
+    // high one, so element j + 8k sits in byte j / 2 + 4k.
+    const int sh = (j & 1) * 4;
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+      const uint32_t q = (blk[2 + (j >> 1) + 4 * k] >> sh) & 15u;
+      w[k] = __fmul_rn(scale, __fsub_rn(__uint_as_float(0x4B000000u | q), 8388616.0f));
+    }
+  } else {  // T_Q5_0, quant.rs:160-186: scale * ((nib | hbit << 4) - 16)
+    const uint32_t qh = lds16(blk + 2) | (lds16(blk + 4) << 16);
+    const uint32_t b0 = blk[6 + j], b1 = blk[6 + j + 8];
+    const uint32_t n4[4] = {b0 & 15, b1 & 15, b0 >> 4, b1 >> 4};
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+      const int e = j + 8 * k;
+      const uint32_t q = n4[k] | (((qh >> e) & 1u) << 4);
+      w[k] = __fmul_rn(scale, __fsub_rn(__uint_as_float(0x4B000000u | q), 8388624.0f));
+    }
+  }
+}
+
+template <int FMT, int MAXB>
+__global__ void __launch_bounds__(CL_THREADS)
+    canon_lane_kernel(const __grid_constant__ CUtensorMap tm, const CnParams p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+  float* xs = reinterpret_cast<float*>(smem + p.off_x);
+  uint8_t* stg = smem + p.off_stage;
+  constexpr int BB = FMT == T_Q8_0 ? 34 : (FMT == T_Q4_0 ? 18 : 22);  // block bytes
+
+  const int tid = threadIdx.x, rr = tid >> 3, j = tid & 7;
+  const int row0 = blockIdx.x * p.rt;
+  const int nrows = min(p.rt, p.R - row0);
+  const int nslab = (p.n + p.slab_e - 1) / p.slab_e;
+
+  if (tid == 0) {
+    for (int i = 0; i < p.nst; i++) mbar_init(&full[i], 1);
+    fence_mbar_init();
+    for (int k = 0; k < min(p.nst, nslab); k++) {
+      mbar_arrive_expect_tx(&full[k], p.stage_b);
+      tma_load_2d(stg + (size_t)k * p.stage_stride, &tm, k * (p.slab_b / 4), row0, &full[k]);
+    }
+  }
+  // Programmatic launch: the weights above never depend on the previous
+  // kernel; x may, so read it only after the previous grid has completed.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  for (int b = 0; b < p.batch; b++)
+    for (int i = tid; i < p.n; i += CL_THREADS) xs[b * p.xs_stride + i] = __ldg(p.x + b * p.ldx + i);
+  __syncthreads();
+
+  float acc[MAXB], chs[MAXB][CN_MAXCH];
+#pragma unroll
+  for (int b = 0; b < MAXB; b++) {
+    acc[b] = 0.0f;
+#pragma unroll
+    for (int c = 0; c < CN_MAXCH; c++) chs[b][c] = 0.0f;
+  }
+  int nch = 0;
+  const bool row_ok = rr < nrows;
+  for (int k = 0; k < nslab; k++) {
+    const int buf = k % p.nst;
+    const bool ok = mbar_wait_bounded(&full[buf], (uint32_t)((k / p.nst) & 1));
+    const int e0 = k * p.slab_e;
+    const int ecount = min(p.slab_e, p.n - e0);
+    if (ok && row_ok) {
+      const uint8_t* row = stg + (size_t)buf * p.stage_stride + (size_t)rr * p.slab_b;
+      const int nblk = ecount >> 5;
+#pragma unroll 4
+      for (int g = 0; g < nblk; g++) {
+        float w[4];
+        lane_weights<FMT>(row + g * BB, j, w);
+        const int e = e0 + 32 * g + j;
+#pragma unroll
+        for (int b = 0; b < MAXB; b++) {
+          if (b < p.batch) {
+            const float* xb = xs + b * p.xs_stride + e;
+#pragma unroll
+            for (int q = 0; q < 4; q++) acc[b] = __fadd_rn(acc[b], __fmul_rn(xb[8 * q], w[q]));
+          }
+        }
+      }
+    }
+    // Close a chunk every 8192 elements and at the row end (quant.rs:557-565):
+    // fixed_tree over the row's 8 lanes, held by 8 consecutive threads.
+    const int e_end = e0 + ecount;
+    if (e_end % 8192 == 0 || e_end == p.n) {
+#pragma unroll
+      for (int b = 0; b < MAXB; b++) {
+        float t = acc[b];
+        float o = __shfl_down_sync(FULL, t, 1);
+        if ((j & 1) == 0) t = __fadd_rn(t, o);
+        o = __shfl_down_sync(FULL, t, 2);
+        if ((j & 3) == 0) t = __fadd_rn(t, o);
+        o = __shfl_down_sync(FULL, t, 4);
+        if (j == 0) t = __fadd_rn(t, o);
+#pragma unroll
+        for (int c = 0; c < CN_MAXCH; c++)
+          if (c == nch) chs[b][c] = t;
+        acc[b] = 0.0f;
+      }
+      nch++;
+    }
+    if (__syncthreads_or(!ok)) {
+      if (tid == 0) {
+        record_error(p.status, KERR_TIMEOUT);
+        for (int i = k; i < min(k + p.nst, nslab); i++)
+          mbar_wait_bounded(&full[i % p.nst], (uint32_t)((i / p.nst) & 1));
+      }
+      return;
+    }
+    if (tid == 0 && k + p.nst < nslab) {
+      mbar_arrive_expect_tx(&full[buf], p.stage_b);
+      tma_load_2d(stg + (size_t)buf * p.stage_stride, &tm, (k + p.nst) * (p.slab_b / 4), row0,
+                  &full[buf]);
+    }
+  }
+  if (row_ok && j == 0) {
+#pragma unroll
+    for (int b = 0; b < MAXB; b++)
+      if (b < p.batch) p.y[(int64_t)b * p.ldy + row0 + rr] = chunk_tree(chs[b], nch);
+  }
+}
+
 // Tensor maps are cached per (pointer, rows, pitch, box).
 struct TmKey {
   const void* ptr;
@@ -355,9 +500,39 @@ cudaError_t launch_fmt(const CUtensorMap& tm, const CnParams& p, int grid, uint3
   return cudaGetLastError();
 }
 
+template <int FMT, int MAXB>
+cudaError_t launch_lane(const CUtensorMap& tm, const CnParams& p, int grid, uint32_t smem,
+                        cudaStream_t st) {
+  static bool attr_set = false;  // once per instantiation
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(canon_lane_kernel<FMT, MAXB>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         max_smem_optin());
+    if (e != cudaSuccess) return e;
+    attr_set = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(CL_THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  kernel_launch_count()++;
+  return cudaLaunchKernelEx(&cfg, canon_lane_kernel<FMT, MAXB>, tm, p);
+}
+
 template <int FMT>
 cudaError_t launch_batch(const CUtensorMap& tm, const CnParams& p, int grid, uint32_t smem,
                          cudaStream_t st) {
+  if constexpr (FMT == T_Q8_0 || FMT == T_Q4_0 || FMT == T_Q5_0) {
+    if (p.batch <= 1) return launch_lane<FMT, 1>(tm, p, grid, smem, st);
+    if (p.batch <= 2) return launch_lane<FMT, 2>(tm, p, grid, smem, st);
+    return launch_lane<FMT, 4>(tm, p, grid, smem, st);
+  }
   if (p.batch <= 1) return launch_fmt<FMT, 1>(tm, p, grid, smem, st);
   if (p.batch <= 2) return launch_fmt<FMT, 2>(tm, p, grid, smem, st);
   return launch_fmt<FMT, 4>(tm, p, grid, smem, st);

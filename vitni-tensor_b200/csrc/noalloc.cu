@@ -20,7 +20,10 @@
 //    every call;
 //  * the first call on a device looks up the array's device address
 //    (cudaGetSymbolAddress, with that device current); make that first call
-//    before any stream capture.
+//    before any stream capture;
+//  * that address is kept for the life of the process: it belongs to the
+//    device's primary context, so a process that resets the device
+//    (cudaDeviceReset) must not call this entry point again afterwards.
 #include <mutex>
 
 #include "../../include/vtq.h"

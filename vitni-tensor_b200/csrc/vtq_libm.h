@@ -17,6 +17,18 @@
 // expf is __host__ __device__ (the device computes SiLU and softmax with it);
 // sinf/cosf/powf run on the host only (RoPE tables are precomputed per position).
 // Host code must be built without FMA contraction (-ffp-contract=off).
+//
+// Notices of the published algorithms these functions restate:
+//   FreeBSD msun (e_expf.c, k_sinf.c, k_cosf.c, e_powf.c, e_rem_pio2f.c):
+//     Copyright (C) 1993 by Sun Microsystems, Inc. All rights reserved.
+//     Developed at SunPro, a Sun Microsystems, Inc. business.
+//     Permission to use, copy, modify, and distribute this software is freely
+//     granted, provided that this notice is preserved.
+//     Float versions by Ian Lance Taylor, Cygnus Support, and Bruce D. Evans.
+//   musl libm (the C sources the Rust `libm` crate ports): Copyright (c)
+//     2005-2020 Rich Felker, et al., MIT licence: permission is granted, free
+//     of charge, to deal in the software without restriction, provided the
+//     copyright notice and this permission notice are included.
 #pragma once
 #include <cmath>
 #include <cstdint>

@@ -133,7 +133,7 @@ MODEL_ID = "vitni-b200-synthetic-tinyllama"
 def synthetic_llama(cfg: dict = TINYLLAMA, seed: int = 0, embd_dtype: int = Q4_K,
                     shared_head: bool = False, arch: str = "llama",
                     qkv_bias: bool = False, wdtypes: dict = None) -> bytes:
-    """Deterministic GGUF for BASELINE config 4: attention/FFN-gate/up weights
+    """Deterministic GGUF of the TinyLlama-shaped decode workload: attention/FFN-gate/up weights
     Q4_K, V / down / output head Q6_K, token_embd Q4_K, norms F32 = 1 + N(0, 0.02).
     arch="qwen2" writes the Qwen2 keys (the reference then uses NeoX RoPE,
     quant_weights.rs:151); qkv_bias adds F32 attn_q/k/v biases ~ N(0, 0.1);

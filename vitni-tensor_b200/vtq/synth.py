@@ -158,7 +158,8 @@ def activation(name: str, batch: int, in_feat: int, seed: int = 0) -> np.ndarray
     return normal(name, seed, batch * in_feat)
 
 
-# Benchmark configurations: (dtype, in_feat, out_feat).
+# Matvec workloads of the benchmark (Q8_0 4096x4096, the Llama-7B FFN pair,
+# the Q6_K output head): (dtype, in_feat, out_feat).
 CONFIGS = {
     "c1_q8_0_4096x4096": [(Q8_0, 4096, 4096)],
     "c2_q4_k_llama7b_ffn": [(Q4_K, 4096, 11008), (Q4_K, 11008, 4096)],
