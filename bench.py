@@ -829,8 +829,8 @@ def main():
                     help="k-quant matvecs: one vtq_linear_list launch per step (default) or "
                          "one vtq_linear launch per matvec")
     ap.add_argument("--per-launch", type=int, default=0,
-                    help="--launch step: consecutive steps per vtq_linear_list launch "
-                         "(0: one rotation of the weight copies)")
+                    help="--launch step: at most this many consecutive steps per "
+                         "vtq_linear_list launch (0: 10); the largest divisor of --steps")
     ap.add_argument("--min-ms", type=float, default=250.0,
                     help="device time of the timed region (graph replays of --steps steps)")
     ap.add_argument("--no-sub", action="store_true",
@@ -927,8 +927,10 @@ def run_matvec(args, ctx, stream, cfg_name, sub=False):
     ys = [torch.empty(r, device="cuda") for dt, n, r in cfg]
     launches_per_step = 1 if mode == "step" else len(cfg)
 
-    per_req = args.per_launch if args.per_launch > 0 else copies
-    per = max(1, min(per_req, vtq.LIST_MAX // len(cfg))) if mode == "step" else 1
+    # Steps per list launch: --per-launch, else the largest divisor of K up to
+    # 10 (so every launch of the timed graph carries the same work).
+    cap = min(args.per_launch if args.per_launch > 0 else 10, vtq.LIST_MAX // len(cfg))
+    per = max(d for d in range(1, cap + 1) if args.steps % d == 0) if mode == "step" else 1
 
     def step(c, events=None, nsteps=1):
         """nsteps consecutive steps from weight copy c on (list mode: one launch)."""

@@ -40,6 +40,9 @@ def _setup(ctx, shapes, tag):
     [(vtq.Q4_K, 4096, 11008), (vtq.Q4_K, 11008, 4096)],          # the Llama-7B FFN pair
     [(vtq.Q6_K, 4096, 3000), (vtq.Q4_K, 256, 1), (vtq.Q6_K, 5632, 147),
      (vtq.Q4_K, 32768, 149), (vtq.Q6_K, 768, 13), (vtq.Q4_K, 2048, 300)],
+    # 33..48 superblocks per row: 16-lane segments of 3 superblocks each.
+    [(vtq.Q6_K, 8448, 700), (vtq.Q4_K, 12288, 301), (vtq.Q6_K, 9216, 37),
+     (vtq.Q4_K, 11008, 1)],
 ])
 def test_independent_items_bit_exact(ctx, shapes):
     import torch

@@ -29,13 +29,22 @@ def test_noalloc_matches_vtq_linear_twice(dtype, n, r, batch):
     torch.cuda.synchronize()
     ctx = vtq.Context(0)
     wt = ctx.upload(dtype, w, n, r)
-    for call in range(2):
-        x = synth.activation(f"noalloc.x{call}", batch, n)
-        ref = ctx.linear(wt, x, batch)
+    xs = [synth.activation(f"noalloc.x{call}", batch, n) for call in range(2)]
+    refs = [ctx.linear(wt, x, batch) for x in xs]
+    # A first call on this device looks up the static array's address (and
+    # CUDA may load the library's device code on first use); after it, the
+    # calls must leave the device's free memory unchanged.
+    y = np.empty(batch * r, np.float32)
+    assert lib.vtq_linear_host_noalloc(dtype, dst.data_ptr(), n, r, xs[0].ctypes.data,
+                                       y.ctypes.data, batch, st) == vtq.OK
+    torch.cuda.synchronize()
+    free0 = torch.cuda.mem_get_info()[0]
+    for call, (x, ref) in enumerate(zip(xs, refs)):
         y = np.full(batch * r, np.nan, np.float32)
         assert lib.vtq_linear_host_noalloc(dtype, dst.data_ptr(), n, r, x.ctypes.data,
                                            y.ctypes.data, batch, st) == vtq.OK
         assert np.array_equal(y.view(np.uint32), ref.view(np.uint32)), f"call {call}"
+    assert torch.cuda.mem_get_info()[0] == free0
     ctx.close()
 
 

@@ -295,28 +295,27 @@ __device__ __forceinline__ void q6k_superblock(const uint8_t* gb, int G, int i, 
 }
 
 // fixed_tree (quant.rs:462-476) over the `len` values of one row held by a
-// segment of `lpr` lanes (value i on segment lane i % 32, chunk i / 32).
+// segment of `lpr` lanes (value i on segment lane i % lpr, chunk i / lpr).
 // Stride-doubling: index i (a multiple of 2^(k+1)) adds index i + 2^k when
-// that index is < len -- the same additions as the reference's level-wise loop.
+// that index is < len -- the same additions as the reference's level-wise
+// loop. Strides below lpr pair lanes of one chunk (shuffles); strides from
+// lpr up pair whole chunks, whose sums sit on segment lane 0.
 template <int NCH>
 __device__ __forceinline__ float seg_fixed_tree(float (&v)[NCH], int sl, int lpr, int len) {
   for (int st = 1; st < lpr; st <<= 1) {
 #pragma unroll
     for (int c = 0; c < NCH; c++) {
       const float o = __shfl_down_sync(FULL, v[c], st);
-      if ((sl & (2 * st - 1)) == 0 && c * 32 + sl + st < len) v[c] = __fadd_rn(v[c], o);
+      if ((sl & (2 * st - 1)) == 0 && c * lpr + sl + st < len) v[c] = __fadd_rn(v[c], o);
     }
   }
-  float r = v[0];
-  if (NCH > 1) {
-    if (32 < len) r = __fadd_rn(r, v[1]);
-    if (NCH > 2) {
-      float r2 = v[2];
-      if (NCH > 3 && 96 < len) r2 = __fadd_rn(r2, v[3]);
-      if (64 < len) r = __fadd_rn(r, r2);
-    }
+#pragma unroll
+  for (int st = 1; st < NCH; st <<= 1) {
+#pragma unroll
+    for (int c = 0; c + st < NCH; c += 2 * st)
+      if ((c + st) * lpr < len) v[c] = __fadd_rn(v[c], v[c + st]);
   }
-  return r;  // valid on segment lane 0
+  return v[0];  // valid on segment lane 0
 }
 
 // One warp pass: rows rr0 + seg of the stage buffer.
@@ -328,7 +327,7 @@ __device__ __forceinline__ void consume_pass(const KqParams& p, const uint8_t* s
   float part[NCH][MAXB];
 #pragma unroll
   for (int c = 0; c < NCH; c++) {
-    const int s = c * 32 + sl;
+    const int s = c * p.lpr + sl;
 #pragma unroll
     for (int b = 0; b < MAXB; b++) part[c][b] = 0.0f;
     if (row_ok && s < p.S) {

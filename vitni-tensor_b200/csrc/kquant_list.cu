@@ -331,13 +331,17 @@ __global__ void __launch_bounds__((CWL + 1) * 32, 1) kq_list_kernel(const __grid
         if (!abort) {
 #endif
           const uint8_t* sbuf = ring + (size_t)grp * P.slot;
-          const int sel = it.qt * 4 + it.nch;
-          if (sel == 1) stage_passes<0, 1>(p, sbuf, st, wig, nrows, r0, sl, seg, xq, xd, bsum);
-          else if (sel == 2) stage_passes<0, 2>(p, sbuf, st, wig, nrows, r0, sl, seg, xq, xd, bsum);
-          else if (sel == 4) stage_passes<0, 4>(p, sbuf, st, wig, nrows, r0, sl, seg, xq, xd, bsum);
-          else if (sel == 5) stage_passes<1, 1>(p, sbuf, st, wig, nrows, r0, sl, seg, xq, xd, bsum);
-          else if (sel == 6) stage_passes<1, 2>(p, sbuf, st, wig, nrows, r0, sl, seg, xq, xd, bsum);
-          else stage_passes<1, 4>(p, sbuf, st, wig, nrows, r0, sl, seg, xq, xd, bsum);
+          const int sel = it.qt * 4 + it.nch;  // nch in 1..4
+          switch (sel) {
+            case 1: stage_passes<0, 1>(p, sbuf, st, wig, nrows, r0, sl, seg, xq, xd, bsum); break;
+            case 2: stage_passes<0, 2>(p, sbuf, st, wig, nrows, r0, sl, seg, xq, xd, bsum); break;
+            case 3: stage_passes<0, 3>(p, sbuf, st, wig, nrows, r0, sl, seg, xq, xd, bsum); break;
+            case 4: stage_passes<0, 4>(p, sbuf, st, wig, nrows, r0, sl, seg, xq, xd, bsum); break;
+            case 5: stage_passes<1, 1>(p, sbuf, st, wig, nrows, r0, sl, seg, xq, xd, bsum); break;
+            case 6: stage_passes<1, 2>(p, sbuf, st, wig, nrows, r0, sl, seg, xq, xd, bsum); break;
+            case 7: stage_passes<1, 3>(p, sbuf, st, wig, nrows, r0, sl, seg, xq, xd, bsum); break;
+            default: stage_passes<1, 4>(p, sbuf, st, wig, nrows, r0, sl, seg, xq, xd, bsum); break;
+          }
         }
         __syncwarp();
         if (lane == 0)
@@ -461,10 +465,21 @@ cudaError_t launch_kq_list(const KqListItem* items, int n, unsigned* counters, u
     it.R = (int)m.out_feat;
     it.S = (int)(m.in_feat / 256);
     it.qt = m.dtype == T_Q4_K ? 0 : 1;
+    // Lanes per row: the power of two covering S when S <= 32; above, the
+    // segment width (8, 16 or 32 lanes, at most 4 superblocks per lane) that
+    // leaves the fewest lane slots idle (S = 43: 16 lanes x 3 = 48 slots, not
+    // 32 x 2 = 64), ties to the wider segment.
     int lpr = 1;
     while (lpr < it.S && lpr < 32) lpr <<= 1;
+    if (it.S > 32) {
+      int best = 32;
+      for (int l = 16; l >= 8; l >>= 1)
+        if ((it.S + l - 1) / l <= 4 && l * ((it.S + l - 1) / l) < best * ((it.S + best - 1) / best))
+          best = l;
+      lpr = best;
+    }
     it.lpr = lpr;
-    it.nch = (it.S + 31) / 32 <= 1 ? 1 : ((it.S + 31) / 32 == 2 ? 2 : 4);
+    it.nch = (it.S + lpr - 1) / lpr;
     it.rows_base = it.R / grid;
     it.rows_rem = it.R % grid;
     it.wait_for = items[i].wait_for;
