@@ -56,14 +56,15 @@ def peaks():
         return 6650.0, "fallback"
 
 
-def profile_traffic(cfg, mode):
-    """DRAM bytes (read + write) per launch of the dominant kernel, from one ncu
-    capture of the same launch (profiles/dram_traffic.json, machine-readable;
-    keyed by workload and launch mode). None when no capture exists."""
+def profile_traffic(cfg, mode, steps_per_launch):
+    """DRAM bytes (read + write) per launch of the dominant kernel: the bytes per
+    step of one ncu capture of the same kernel on the same workload
+    (profiles/dram_traffic.json, machine-readable, keyed by workload and launch
+    mode) times the steps one launch processes. None when no capture exists."""
     try:
         with open(os.path.join(REPO, "profiles", "dram_traffic.json")) as f:
             t = json.load(f).get(f"{cfg}/{mode}")
-        return None if t is None else float(t["dram_bytes_per_launch"])
+        return None if t is None else float(t["dram_bytes_per_step"]) * steps_per_launch
     except (OSError, ValueError, KeyError):
         return None
 
@@ -588,7 +589,8 @@ def run_sharded(args, world, rank, local, ctx, stream, cfg):
     fused = all(dt in (vtq.Q4_K, vtq.Q6_K) for dt, n, r in cfg) and world <= 8 and \
         os.environ.get("VTQ_GATHER", "fused") == "fused"
     use_list = fused and args.launch == "step"
-    per = max(1, min(copies, vtq.LIST_MAX // len(cfg))) if use_list else 1
+    cap = min(args.per_launch if args.per_launch > 0 else 10, vtq.LIST_MAX // len(cfg))
+    per = max(d for d in range(1, cap + 1) if args.steps % d == 0) if use_list else 1
     steps = max(copies, min(args.steps, 2000)) // copies * copies
     offs = [sum(rows_log[:i]) for i in range(len(cfg))]
     if fused:
@@ -917,7 +919,7 @@ def run_matvec(args, ctx, stream, cfg_name, sub=False):
     step_bytes = sum(algo_bytes(dt, n, r) for dt, n, r in cfg)
     wbytes = sum(r * vtq.row_bytes(dt, n) for dt, n, r in cfg)
     copies = max(1, -(-ROTATE_MIN_BYTES // wbytes))
-    if args.launches_only:
+    if args.launches_only and mode != "step":
         copies = 1
     host_w = [synth.weight(dt, f"{cfg_name}.w.{n}x{r}", r, n) for dt, n, r in cfg]
     host_x = [synth.activation(f"{cfg_name}.x.{n}", 1, n) for dt, n, r in cfg]
@@ -1013,7 +1015,7 @@ def run_matvec(args, ctx, stream, cfg_name, sub=False):
     avg_ms = med / n_launch
     peak, peak_kind = peaks()
     achieved = per_launch_bytes / (avg_ms / 1e3) / 1e9
-    traffic = profile_traffic(cfg_name, mode)
+    traffic = profile_traffic(cfg_name, mode, K / n_launch)
 
     # ---- e2e through the public C ABI with host buffers ----
     # Each of the `per` steps a call covers has its own page-locked x and y.
