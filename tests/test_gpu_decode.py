@@ -106,3 +106,18 @@ def test_decode_errors():
     with pytest.raises(vtq.Internal, match="must not be empty"):
         sess.run([], 3)
     sess.close()
+
+
+def test_long_context_attention_bit_exact(monkeypatch):
+    """seq_len 16384: the attention kernel's shared memory (3 head sizes plus one
+    score per cached position, (3 * 64 + 16384) * 4 B = 66 KB) is above the
+    48 KB default, so the session opts the kernel into the larger limit. The
+    positions run are few; the allocation and the opt-in are what is tested."""
+    for k in ("VTQ_DECODE_PERSISTENT", "VTQ_DECODE_UNFUSED", "VTQ_DECODE_NO_PREFILL"):
+        monkeypatch.delenv(k, raising=False)
+    cfg = dict(SMALL, seq_len=16384)
+    blob = gguf.synthetic_llama(cfg, seed=5)
+    prompt = gguf.prompt_tokens(6, cfg["vocab"], seed=2)
+    got, lg, again, ref, rlg = run_both(blob, prompt, 5)
+    assert_bits(lg, rlg)
+    assert list(got) == list(ref) and list(again) == list(ref)
