@@ -44,8 +44,10 @@ __device__ unsigned long long g_mk_trace[5][1024];
 
 constexpr int MK_CW = 15;  // consumer warps (16 warps in all: 128 registers a thread)
 constexpr int MK_THREADS = (MK_CW + 1) * 32;
-constexpr int MK_NST_MAX = 16;          // ring slots
-constexpr uint32_t MK_SLOT = 24576;     // bytes per ring slot (whole warp passes)
+constexpr int MK_NST_MAX = 16;          // barrier array size
+constexpr int MK_NSLOT = 5;             // ring slots; slot j is consumed by warp group j only
+constexpr int MK_WPG = MK_CW / MK_NSLOT;  // warps per slot group
+static_assert(MK_CW % MK_NSLOT == 0, "slot groups");
 
 enum : int { PH_EMBED = 0, PH_NORM = 1, PH_MATVEC = 2, PH_ATTN = 3, PH_ARGMAX = 4 };
 enum : int { XS_GLOBAL = 0, XS_NORMED = 1 };
@@ -86,6 +88,7 @@ struct MkArgs {
   uint32_t* out_tokens;
   // shared-memory layout
   int nst;
+  uint32_t slot_bytes;
   uint32_t off_xn, off_xsq, off_xscr, off_xd, off_bsum, off_xq, off_ring;
 };
 
@@ -121,7 +124,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_mk_kernel(const MkArgs a
   if (tid == 0) {
     for (int i = 0; i < a.nst; i++) {
       mbar_init(&full[i], 1);
-      mbar_init(&empty[i], MK_CW);
+      mbar_init(&empty[i], MK_WPG);
     }
     fence_mbar_init();
     s_abort = 0;
@@ -152,7 +155,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_mk_kernel(const MkArgs a
           const int ra = k * p.rps, rb = min(ra + p.rps, nrows);
           const uint32_t bytes = (uint32_t)((rb - ra) * p.pitch);
           mbar_arrive_expect_tx(&full[slot], bytes);
-          bulk_g2s_stream(ring + (size_t)slot * MK_SLOT, p.W + (int64_t)(r0 + ra) * p.pitch, bytes,
+          bulk_g2s_stream(ring + (size_t)slot * a.slot_bytes, p.W + (int64_t)(r0 + ra) * p.pitch, bytes,
                           &full[slot], pol);
         }
       }
@@ -209,36 +212,36 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_mk_kernel(const MkArgs a
       const int nstages = (nrows + p.rps - 1) / p.rps;
       const int rpw = 32 / p.lpr;
       const int seg = lane / p.lpr, sl = lane - seg * p.lpr;
-      const int gps = p.rps / rpw;
-      const int ngroups = (nrows + rpw - 1) / rpw;
-      int g = warp;
-      for (int k = 0; k < nstages; k++, gs++) {
-        const int slot = gs % a.nst, use = gs / a.nst;
-        // Every warp waits for every stage in order (parity waits are only
-        // unambiguous one phase ahead; this also keeps the CTA alive until
-        // its bulk copies have landed).
-        if (!mbar_wait_bounded(&full[slot], (uint32_t)(use & 1))) {
+      const int grp = warp / MK_WPG, wig = warp - grp * MK_WPG;
+      // Stage gs + k sits in slot (gs + k) % nst and is consumed by that slot's
+      // warp group alone, which waits for the slot's phases in order.
+      int k = (grp - (int)(gs % a.nst)) % a.nst;
+      if (k < 0) k += a.nst;
+      for (; k < nstages; k += a.nst) {
+        const uint32_t kk = gs + k;
+        if (!mbar_wait_bounded(&full[grp], (uint32_t)((kk / a.nst) & 1))) {
           if (lane == 0) record_error(a.status, KERR_TIMEOUT);
           s_abort = 1;
         }
-        const int gend = min((k + 1) * gps, ngroups);
-        const uint8_t* sbuf = ring + (size_t)slot * MK_SLOT;
+        const uint8_t* sbuf = ring + (size_t)grp * a.slot_bytes;
         if (!s_abort) {
-          for (; g < gend; g += MK_CW) {
-            const int r = g * rpw + seg;
+          const int rows = min(p.rps, nrows - k * p.rps);
+          for (int pr = wig * rpw; pr < rows; pr += MK_WPG * rpw) {
+            const int r = k * p.rps + pr + seg;
             if (ph.qt == 0)
-              consume_pass<0, 1, 1>(p, sbuf, r - k * p.rps, r < nrows, sl, r0 + r, xq, xd, bsum,
+              consume_pass<0, 1, 1>(p, sbuf, pr + seg, pr + seg < rows, sl, r0 + r, xq, xd, bsum,
                                     nullptr, 0);
             else
-              consume_pass<1, 1, 1>(p, sbuf, r - k * p.rps, r < nrows, sl, r0 + r, xq, xd, bsum,
+              consume_pass<1, 1, 1>(p, sbuf, pr + seg, pr + seg < rows, sl, r0 + r, xq, xd, bsum,
                                     nullptr, 0);
           }
         }
         __syncwarp();
         if (lane == 0)
-          asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&empty[slot]))
+          asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&empty[grp]))
                        : "memory");
       }
+      gs += nstages;
       cons_sync();  // the next phase reuses xq / xd / bsum
     } else if (ph.kind == PH_ATTN) {
       if (bid < a.n_heads)
@@ -369,8 +372,9 @@ cudaError_t mk_build(const MkModel& m, MkPlan** out) {
   int optin = 0, dev = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-  const int nst = std::min<int>(MK_NST_MAX, (optin - (int)off_ring) / (int)MK_SLOT);
-  if (nst < 2) {
+  const int nst = MK_NSLOT;
+  const uint32_t MK_SLOT = (uint32_t)((optin - (int)off_ring) / nst) / 128 * 128;
+  if (MK_SLOT < 8192) {
     delete plan;
     return cudaErrorInvalidValue;
   }
@@ -511,6 +515,7 @@ cudaError_t mk_build(const MkModel& m, MkPlan** out) {
   a.prompt = m.prompt;
   a.out_tokens = m.out_tokens;
   a.nst = nst;
+  a.slot_bytes = MK_SLOT;
   a.off_xn = off_xn;
   a.off_xsq = off_xsq;
   a.off_xscr = off_xscr;
