@@ -92,6 +92,7 @@ __device__ long long g_gemm_trace[64][8];
 
 struct GemmParams {
   int M, n, S, R;
+  int tiles_m, ntiles;  // token tiles; work units (token tile fastest, then row tile)
   float* y;
   int64_t ldy;
   const float* xd;  // [S][M] activation block scales (token-major per superblock)
@@ -218,8 +219,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   float2* meta = reinterpret_cast<float2*>(gbase + OFF_META);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int tok0 = blockIdx.x * GM, row0 = blockIdx.y * GR;
   const int S = p.S;
+  // Persistent CTAs: unit u covers tokens [GM (u mod tiles_m), +GM) and rows
+  // [GR (u div tiles_m), +GR). Every role walks the same units and counts
+  // superblock steps g across them, so the pipeline (stages, TMEM buffers,
+  // barrier phases) runs on from one unit into the next.
 
   if (tid == 0) {
     auto init = [](uint32_t b, unsigned c) {
@@ -252,31 +256,37 @@ __global__ void __launch_bounds__(kThreads, 1)
     asm volatile("setmaxnreg.dec.sync.aligned.u32 56;");
     // ---- producer ----
     if (lane == 0) {
-      for (int s = 0; s < S && !*abort_flag; s++) {
-        const int sx = s % NX, sw = s % NW;
-        if (!wait_u32(X_EMPTY(sx), ((s / NX) + 1) & 1)) { fail(); break; }
+      int g = 0;
+      for (int u = blockIdx.x; u < p.ntiles && !*abort_flag; u += gridDim.x) {
+      const int tok0 = (u % p.tiles_m) * GM, row0 = (u / p.tiles_m) * GR;
+      for (int s = 0; s < S && !*abort_flag; s++, g++) {
+        const int sx = g % NX, sw = g % NW;
+        if (!wait_u32(X_EMPTY(sx), ((g / NX) + 1) & 1)) { fail(); break; }
         mbar_arrive_expect_tx(reinterpret_cast<uint64_t*>(gbase + OFF_BAR + 8 * sx), X_STAGE);
         const uint32_t xs = base + OFF_X + sx * X_STAGE;
         tma_load_2d(xs, &tmx, 256 * s, tok0, X_FULL(sx));
         tma_load_2d(xs + X_STAGE / 2, &tmx, 256 * s + 128, tok0, X_FULL(sx));
-        if (!wait_u32(W_EMPTY(sw), ((s / NW) + 1) & 1)) { fail(); break; }
+        if (!wait_u32(W_EMPTY(sw), ((g / NW) + 1) & 1)) { fail(); break; }
         mbar_arrive_expect_tx(reinterpret_cast<uint64_t*>(gbase + OFF_BAR + 8 * (2 * NX + sw)),
                               W_STAGE);
         tma_load_2d(base + OFF_W + sw * W_STAGE, &tmw, 144 * s, row0, W_FULL(sw));
         GT(0, s);
+      }
       }
     }
   } else if (warp == 1) {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 56;");
     // ---- MMA issuer ----
     if (lane == 0) {
-      for (int s = 0; s < S && !*abort_flag; s++) {
-        const int sx = s % NX, sp = s % NP, ab = s % NA;
-        bool ok = wait_u32(X_FULL(sx), (s / NX) & 1);
+      const int nsteps = ((p.ntiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x) * S;
+      for (int g = 0; g < nsteps && !*abort_flag; g++) {
+        const int s = g % S;
+        const int sx = g % NX, sp = g % NP, ab = g % NA;
+        bool ok = wait_u32(X_FULL(sx), (g / NX) & 1);
         GT(6, s);
-        ok = ok && wait_u32(P_FULL(sp), (s / NP) & 1);
+        ok = ok && wait_u32(P_FULL(sp), (g / NP) & 1);
         GT(7, s);
-        if (!ok || !wait_u32(A_EMPTY(ab), ((s / NA) + 1) & 1)) {
+        if (!ok || !wait_u32(A_EMPTY(ab), ((g / NA) + 1) & 1)) {
           fail();
           break;
         }
@@ -303,11 +313,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     // 8 consecutive lanes take 8 consecutive rows so that their 16-byte plane
     // stores land in 8 different swizzled slots of a 128-byte line ----
     const int t = tid - 32 * kBuildWarp0, r = t & 31, jp = t >> 5;
-    for (int s = 0; s < S && !*abort_flag; s++) {
-      const int sw = s % NW, sp = s % NP, sm = s % NMETA;
+    const int nsteps = ((p.ntiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x) * S;
+    for (int g = 0; g < nsteps && !*abort_flag; g++) {
+      const int s = g % S;
+      const int sw = g % NW, sp = g % NP, sm = g % NMETA;
       if (t == 0) GT(5, s);
-      if (!wait_u32(W_FULL(sw), (s / NW) & 1) || !wait_u32(P_EMPTY(sp), ((s / NP) + 1) & 1) ||
-          !wait_u32(M_EMPTY(sm), ((s / NMETA) + 1) & 1)) {
+      if (!wait_u32(W_FULL(sw), (g / NW) & 1) || !wait_u32(P_EMPTY(sp), ((g / NP) + 1) & 1) ||
+          !wait_u32(M_EMPTY(sm), ((g / NMETA) + 1) & 1)) {
         fail();
         break;
       }
@@ -367,20 +379,23 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---- epilogue: thread = token (TMEM lane), 16 weight rows ----
     const int ew = warp - kEpiWarp0;
     const int q = warp & 3, half = ew >> 2;
+    const int rbase = 16 * half;
+    int g = 0;
+    for (int u = blockIdx.x; u < p.ntiles && !*abort_flag; u += gridDim.x) {
+    const int tok0 = (u % p.tiles_m) * GM, row0 = (u / p.tiles_m) * GR;
     const int b = tok0 + 32 * q + lane;
     const bool bvalid = b < p.M;
-    const int rbase = 16 * half;
     float st[LV][16];
 #pragma unroll
     for (int L = 0; L < LV; L++)
 #pragma unroll
       for (int i = 0; i < 16; i++) st[L][i] = 0.0f;
     float xd_next = bvalid ? p.xd[b] : 0.0f;
-    for (int s = 0; s < S && !*abort_flag; s++) {
-      const int ab = s % NA, sm = s % NMETA;
+    for (int s = 0; s < S && !*abort_flag; s++, g++) {
+      const int ab = g % NA, sm = g % NMETA;
       const float xdv = xd_next;
       if (s + 1 < S) xd_next = bvalid ? p.xd[(int64_t)(s + 1) * p.M + b] : 0.0f;
-      if (!wait_u32(A_FULL(ab), (s / NA) & 1) || !wait_u32(M_FULL(sm), (s / NMETA) & 1)) {
+      if (!wait_u32(A_FULL(ab), (g / NA) & 1) || !wait_u32(M_FULL(sm), (g / NMETA) & 1)) {
         if (lane == 0) fail();
         break;
       }
@@ -433,6 +448,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int o = row0 + rbase + i;
         if (o < p.R) p.y[(int64_t)b * p.ldy + o] = acc;
       }
+    }
     }
   }
   tc_fence_before();
@@ -607,8 +623,10 @@ cudaError_t launch_kq_gemm(const DevMatrix& m, const float* x, int64_t ldx, int6
   if ((e = byte_map(&tmw, m.data, R, m.pitch, m.pitch, 144, GR, CU_TENSOR_MAP_SWIZZLE_NONE)) !=
       cudaSuccess)
     return e;
-  GemmParams p{M, n, S, R, y, ldy, xd, status};
-  const dim3 grid((unsigned)((M + GM - 1) / GM), (unsigned)((R + GR - 1) / GR));
+  const int tiles_m = (M + GM - 1) / GM, ntiles = tiles_m * ((R + GR - 1) / GR);
+  GemmParams p{M, n, S, R, tiles_m, ntiles, y, ldy, xd, status};
+  // Persistent: at most one CTA per SM, each walking units gridDim.x apart.
+  const dim3 grid((unsigned)std::min(ntiles, num_sms()));
   // Levels of the fixed-tree counter: floor(log2 S) + 1.
   int lv = 1;
   while ((1 << lv) <= S) lv++;
