@@ -84,7 +84,7 @@ constexpr uint32_t SMEM_BYTES = OFF_SLOT + 16 + 1024;  // + alignment slack
 __device__ long long g_gemm_trace[64][8];
 #define GT(slot, s_)                                                              \
   do {                                                                            \
-    if (blockIdx.x == 0 && blockIdx.y == 1 && (s_) < 64) g_gemm_trace[s_][slot] = clock64(); \
+    if (blockIdx.x == 0 && (s_) < 64) g_gemm_trace[s_][slot] = clock64(); \
   } while (0)
 #else
 #define GT(slot, s_) (void)0
@@ -270,7 +270,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_arrive_expect_tx(reinterpret_cast<uint64_t*>(gbase + OFF_BAR + 8 * (2 * NX + sw)),
                               W_STAGE);
         tma_load_2d(base + OFF_W + sw * W_STAGE, &tmw, 144 * s, row0, W_FULL(sw));
-        GT(0, s);
+        GT(0, g);
       }
       }
     }
@@ -283,15 +283,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int s = g % S;
         const int sx = g % NX, sp = g % NP, ab = g % NA;
         bool ok = wait_u32(X_FULL(sx), (g / NX) & 1);
-        GT(6, s);
+        GT(6, g);
         ok = ok && wait_u32(P_FULL(sp), (g / NP) & 1);
-        GT(7, s);
+        GT(7, g);
         if (!ok || !wait_u32(A_EMPTY(ab), ((g / NA) + 1) & 1)) {
           fail();
           break;
         }
         tc_fence_after();
-        GT(2, s);
+        GT(2, g);
         const uint32_t xs = base + OFF_X + sx * X_STAGE, ps = base + OFF_P + sp * P_STAGE;
         const uint32_t d = tmem + (uint32_t)ab * 128u;
 #pragma unroll
@@ -317,7 +317,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int g = 0; g < nsteps && !*abort_flag; g++) {
       const int s = g % S;
       const int sw = g % NW, sp = g % NP, sm = g % NMETA;
-      if (t == 0) GT(5, s);
+      if (t == 0) GT(5, g);
       if (!wait_u32(W_FULL(sw), (g / NW) & 1) || !wait_u32(P_EMPTY(sp), ((g / NP) + 1) & 1) ||
           !wait_u32(M_EMPTY(sm), ((g / NMETA) + 1) & 1)) {
         fail();
@@ -369,7 +369,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       // Generic-proxy stores -> visible to the tensor core (async proxy).
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      if (t == 0) GT(1, s);
+      if (t == 0) GT(1, g);
       mbar_arrive(P_FULL(sp));
       mbar_arrive(M_FULL(sm));
       mbar_arrive(W_EMPTY(sw));
@@ -381,26 +381,32 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int q = warp & 3, half = ew >> 2;
     const int rbase = 16 * half;
     int g = 0;
+    // Token of this thread in unit u; the first block scale of the CTA's first
+    // unit, then of each next unit during the current unit's last step.
+    auto token_of = [&](int u) { return (u % p.tiles_m) * GM + 32 * q + lane; };
+    float xd_next = 0.0f;
+    if ((int)blockIdx.x < p.ntiles && token_of(blockIdx.x) < p.M) xd_next = p.xd[token_of(blockIdx.x)];
     for (int u = blockIdx.x; u < p.ntiles && !*abort_flag; u += gridDim.x) {
     const int tok0 = (u % p.tiles_m) * GM, row0 = (u / p.tiles_m) * GR;
     const int b = tok0 + 32 * q + lane;
     const bool bvalid = b < p.M;
+    const int un = u + gridDim.x, bn = un < p.ntiles ? token_of(un) : p.M;
     float st[LV][16];
 #pragma unroll
     for (int L = 0; L < LV; L++)
 #pragma unroll
       for (int i = 0; i < 16; i++) st[L][i] = 0.0f;
-    float xd_next = bvalid ? p.xd[b] : 0.0f;
     for (int s = 0; s < S && !*abort_flag; s++, g++) {
       const int ab = g % NA, sm = g % NMETA;
       const float xdv = xd_next;
       if (s + 1 < S) xd_next = bvalid ? p.xd[(int64_t)(s + 1) * p.M + b] : 0.0f;
+      else xd_next = bn < p.M ? p.xd[bn] : 0.0f;
       if (!wait_u32(A_FULL(ab), (g / NA) & 1) || !wait_u32(M_FULL(sm), (g / NMETA) & 1)) {
         if (lane == 0) fail();
         break;
       }
       tc_fence_after();
-      if (ew == 0 && lane == 0) GT(3, s);
+      if (ew == 0 && lane == 0) GT(3, g);
       float part[16];
 #pragma unroll
       for (int hh = 0; hh < 2; hh++) {
@@ -424,7 +430,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // 2^L leaves while bit L of the number of leaves seen (s) is set. Leaf s
       // merges with the levels below the lowest clear bit of s (warp-uniform).
       tree_push<LV>(st, part, __ffs(~s) - 1);
-      if (ew == 0 && lane == 0) GT(4, s);
+      if (ew == 0 && lane == 0) GT(4, g);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {
@@ -434,6 +440,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     if (!*abort_flag && bvalid) {
       // Remaining subtrees sit at the set bits of S; fold them right to left.
+      float out[16];
 #pragma unroll
       for (int i = 0; i < 16; i++) {
         float acc = 0.0f;
@@ -445,8 +452,20 @@ __global__ void __launch_bounds__(kThreads, 1)
             have = true;
           }
         }
-        const int o = row0 + rbase + i;
-        if (o < p.R) p.y[(int64_t)b * p.ldy + o] = acc;
+        out[i] = acc;
+      }
+      // This thread's 16 consecutive outputs of token b: four 16-byte stores
+      // when they are whole and aligned, else one by one.
+      const int o0 = row0 + rbase;
+      float* yr = p.y + (int64_t)b * p.ldy + o0;
+      if (o0 + 16 <= p.R && (reinterpret_cast<uintptr_t>(yr) & 15u) == 0) {
+#pragma unroll
+        for (int i = 0; i < 16; i += 4)
+          *reinterpret_cast<float4*>(yr + i) = make_float4(out[i], out[i + 1], out[i + 2], out[i + 3]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 16; i++)
+          if (o0 + i < p.R) yr[i] = out[i];
       }
     }
     }
@@ -584,6 +603,13 @@ cudaError_t launch_lv(const CUtensorMap& tmx, const CUtensorMap& tmw, const Gemm
 }
 
 }  // namespace
+
+#ifdef VTQ_GEMM_TRACE
+// Diagnostic build only: the per-role clock64 stamps of CTA 0's first 64 steps.
+extern "C" int vtq_gemm_trace(long long* out) {
+  return (int)cudaMemcpyFromSymbol(out, g_gemm_trace, sizeof(long long) * 64 * 8);
+}
+#endif
 
 bool kq_gemm_supported(const DevMatrix& m, int64_t batch) {
   return m.dtype == T_Q4_K && batch >= 1 && batch <= (int64_t)INT32_MAX / 2 && m.in_feat % 256 == 0 &&
