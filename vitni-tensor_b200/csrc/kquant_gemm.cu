@@ -313,6 +313,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     // 8 consecutive lanes take 8 consecutive rows so that their 16-byte plane
     // stores land in 8 different swizzled slots of a 128-byte line ----
     const int t = tid - 32 * kBuildWarp0, r = t & 31, jp = t >> 5;
+    // This thread's 12 plane offsets (3 planes x 2 sub-blocks x 2 halves) are
+    // the same for every superblock.
+    uint32_t poff[2][2][3];
+#pragma unroll
+    for (int h16 = 0; h16 < 2; h16++)
+#pragma unroll
+      for (int e = 0; e < 2; e++) {
+        const int k = 32 * (2 * jp + e) + 16 * h16;
+        poff[h16][e][0] = plane_off(r, k);
+        poff[h16][e][1] = plane_off(GR + r, k);
+        poff[h16][e][2] = plane_off(2 * GR + r, k);
+      }
     const int nsteps = ((p.ntiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x) * S;
     for (int g = 0; g < nsteps && !*abort_flag; g++) {
       const int s = g % S;
@@ -359,11 +371,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             lo[u] = nib * sl;  // byte products <= 105: no carries between bytes
             hi[u] = nib * sh;
           }
-          const int k = 32 * (2 * jp + e) + 16 * h16;
           const uint32_t mrep = mn[e] * 0x01010101u;
-          *reinterpret_cast<uint4*>(pl + plane_off(r, k)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-          *reinterpret_cast<uint4*>(pl + plane_off(GR + r, k)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-          *reinterpret_cast<uint4*>(pl + plane_off(2 * GR + r, k)) = make_uint4(mrep, mrep, mrep, mrep);
+          *reinterpret_cast<uint4*>(pl + poff[h16][e][0]) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+          *reinterpret_cast<uint4*>(pl + poff[h16][e][1]) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+          *reinterpret_cast<uint4*>(pl + poff[h16][e][2]) = make_uint4(mrep, mrep, mrep, mrep);
         }
       }
       }
