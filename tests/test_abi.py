@@ -84,3 +84,12 @@ def test_workspace_query_without_gpu():
     assert lib.vtq_linear_device_workspace_bytes(vtq.Q4_K, 4096, 1, 0) == 0
     assert lib.vtq_linear_device_workspace_bytes(vtq.Q6_K, 4096, 32, 0) == 0
     assert lib.vtq_linear_device_workspace_bytes(vtq.Q4_K, 4096, 32, vtq.Q4K_FLOAT) == 0
+
+
+def test_list_entry_points_validate_without_gpu():
+    """vtq_linear_list / vtq_linear_list_gather reject a missing context or
+    list before touching the device."""
+    lib = vtq.load_library()
+    assert lib.vtq_linear_list(None, None, 1, 0) == vtq.ERR_INVALID_ARG
+    assert lib.vtq_linear_list_gather(None, None, 1, None, 0, 0) == vtq.ERR_INVALID_ARG
+    assert lib.vtq_set_wait_limit(None, 1000) == vtq.ERR_INVALID_ARG

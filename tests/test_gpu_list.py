@@ -121,6 +121,13 @@ def test_list_validation(ctx):
         ctx.linear_list([(w4, 16, 16, 0)])  # wait_for must name an earlier item
     with pytest.raises(vtq.InvalidArg):
         ctx.linear_list([(w4, 16, 16)] * (vtq.LIST_MAX + 1))
+    # Host pointers cannot name an earlier item's y as x.
+    x = np.zeros(256, np.float32)
+    y = np.zeros(8, np.float32)
+    with pytest.raises(vtq.InvalidArg):
+        ctx.linear_list([(w4, x.ctypes.data, y.ctypes.data),
+                         (w4, x.ctypes.data, y.ctypes.data + 16, 0)],
+                        host=True)
 
 
 @pytest.mark.parametrize("pinned", [True, False])
